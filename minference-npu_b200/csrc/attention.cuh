@@ -1,0 +1,110 @@
+// Sparse FlashAttention forward for sm_100a: one kernel serves all three
+// MInference patterns plus dense causal attention.
+//
+// Work unit: one CTA = one (batch, head, 128-row query tile).  The tile walks
+// a list of 64-key KV blocks ("entries"); each entry carries one 64-bit
+// column mask per 64-row half of the query tile, so the kernel computes the
+// exact token-level visible set of every pattern:
+//   * stream_llm / dense (mode 0): entries are generated arithmetically
+//     (sink blocks, then the band blocks that are not sink blocks); sink and
+//     window predicates are evaluated per element, so the sink and local
+//     partial softmaxes merge inside one online softmax (no LSE merge pass).
+//   * block_sparse and vertical_and_slash (mode 1): entries come from a plan
+//     written by the index kernels (block_sparse.cu / vs_index.cu).
+// Causality (key <= absolute query position) is always applied per element.
+//
+// Warp roles (192 threads):
+//   warps 0-3  softmax: thread r owns query row r of the tile; reads S from
+//              TMEM, applies masks, online softmax in registers (exp2),
+//              writes P (bf16/fp16) to shared memory, rescales O in TMEM when
+//              the running max grows by more than 2^8, final normalisation.
+//   warp 4     TMA producer: Q once, then K and V blocks into a 2-stage ring.
+//   warp 5     TMEM allocator + single-thread tcgen05.mma issuer:
+//              S = Q K^T (M=128, N=64, K=D) into a double-buffered TMEM tile,
+//              O += P V (M=128, N=D, K=64) into TMEM.
+#pragma once
+#include "common.cuh"
+
+namespace mib200 {
+
+struct PlanEntry {
+  int32_t kb;   // key block index (keys [64*kb, 64*kb+64))
+  int32_t pad;
+  uint64_t m0;  // visible-column mask for query rows [0,64) of the tile
+  uint64_t m1;  // visible-column mask for query rows [64,128) of the tile
+};
+static_assert(sizeof(PlanEntry) == 24, "PlanEntry layout");
+
+// Entries of query tile t start at plan_offset(t, cap) inside a head's plan:
+// tile t holds at most min(2t+2, cap) entries (cap even).
+__host__ __device__ __forceinline__ int64_t plan_offset(int64_t t, int64_t cap) {
+  const int64_t t0 = cap / 2;
+  if (t <= t0) return t * (t + 1);
+  return t0 * (t0 + 1) + (t - t0) * cap;
+}
+
+struct AttnParams {
+  int B, H, Sq, Sk;
+  int q_off;           // Sk - Sq: absolute position of query row 0
+  int T;               // number of 128-row query tiles
+  int mode;            // 0: stream/dense arithmetic entries, 1: plan entries
+  long long n_init;    // sink length (mode 0; 0 in mode 1)
+  long long n_local;   // window length (mode 0; Sk+1 in mode 1)
+  float scale_log2;    // softmax_scale * log2(e)
+  void* out;
+  long long os_b, os_h, os_s;  // output element strides
+  const PlanEntry* plan;       // mode 1
+  const int* plan_count;       // mode 1: [B*H][T]
+  long long plan_cap;          // mode 1
+  long long plan_head_stride;  // mode 1: entries per (b,h)
+};
+
+constexpr int kBM = 128;       // query rows per CTA
+constexpr int kBN = 64;        // keys per KV block
+constexpr int kStages = 2;     // KV ring depth
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 256;  // S0 [0,64), S1 [64,128), O [128,128+D)
+
+template <int D>
+struct AttnSmem {
+  static constexpr int NC = D / 32;                 // 64-byte chunks per row
+  static constexpr int kQBytes = NC * kBM * 64;     // Q tile
+  static constexpr int kKVBytes = NC * kBN * 64;    // one K (or V) block
+  static constexpr int kPBytes = 2 * kBM * 64;      // one P buffer (64 keys)
+  static constexpr int kQOff = 0;
+  static constexpr int kKOff = kQOff + kQBytes;
+  static constexpr int kVOff = kKOff + kStages * kKVBytes;
+  static constexpr int kPOff = kVOff + kStages * kKVBytes;
+  static constexpr int kBarOff = kPOff + 2 * kPBytes;
+  // barriers: q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], pv_done[2]
+  static constexpr int kNumBars = 1 + 2 * kStages + 6;
+  static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
+  static constexpr int kAbortOff = kTmemSlotOff + 4;
+  static constexpr int kBytes = kAbortOff + 4;
+  static constexpr int kAlloc = kBytes + 1024;      // room to align the base to 1 KiB
+};
+
+// Entry j of the current tile (identical result in every warp that asks).
+struct EntrySource {
+  int mode;
+  // mode 0
+  int nsb;         // number of sink blocks
+  int band_start;  // first band block after the sink blocks
+  // mode 1
+  const PlanEntry* list;
+
+  __device__ __forceinline__ void get(int j, int& kb, uint64_t& m0, uint64_t& m1) const {
+    if (mode == 0) {
+      kb = (j < nsb) ? j : band_start + (j - nsb);
+      m0 = ~0ull;
+      m1 = ~0ull;
+    } else {
+      const PlanEntry e = list[j];
+      kb = e.kb;
+      m0 = e.m0;
+      m1 = e.m1;
+    }
+  }
+};
+
+}  // namespace mib200

@@ -1,0 +1,47 @@
+// C ABI entry points that are not tied to one pattern: version, device error
+// word, and the stream_llm / dense causal attention.
+#include "attention.cuh"
+#include "host_util.h"
+
+namespace mib200 {
+int launch_attention(const mi_tensor4& q, const mi_tensor4& k, const mi_tensor4& v,
+                     const mi_tensor4& out, int64_t D, int dtype, AttnParams prm,
+                     cudaStream_t stream);
+}  // namespace mib200
+
+using namespace mib200;
+
+extern "C" const char* mi_version(void) { return "minference-b200 0.1.0 (sm_100a)"; }
+
+extern "C" int mi_get_device_error(int* code) {
+  if (!code) return MI_ERR_SHAPE;
+  if (cudaDeviceSynchronize() != cudaSuccess) return MI_ERR_LAUNCH;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) return MI_ERR_LAUNCH;
+  const int zero = 0;
+  if (cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)) != cudaSuccess) return MI_ERR_LAUNCH;
+  *code = v;
+  return MI_OK;
+}
+
+extern "C" int mi_stream_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor4 out, int64_t B,
+                             int64_t H, int64_t S_q, int64_t S_k, int64_t D, int dtype,
+                             int64_t n_init, int64_t n_local, float softmax_scale, void* stream) {
+  if (dtype != MI_F16 && dtype != MI_BF16) return MI_ERR_DTYPE;
+  if (D != 64 && D != 96 && D != 128) return MI_ERR_SHAPE;
+  if (B < 0 || H < 0 || S_q < 0 || S_k < 0 || S_q > S_k || S_k > (1 << 30)) return MI_ERR_SHAPE;
+  if (B > 65535 || H > 65535) return MI_ERR_SHAPE;
+  if (B == 0 || H == 0 || S_q == 0) return MI_OK;
+  AttnParams prm{};
+  prm.B = (int)B;
+  prm.H = (int)H;
+  prm.Sq = (int)S_q;
+  prm.Sk = (int)S_k;
+  prm.q_off = (int)(S_k - S_q);
+  prm.T = (int)((S_q + 127) / 128);
+  prm.mode = 0;
+  prm.n_init = n_init < 0 ? 0 : (n_init > S_k ? S_k : n_init);
+  prm.n_local = n_local < 0 ? 0 : (n_local > S_k + 1 ? S_k + 1 : n_local);
+  prm.scale_log2 = softmax_scale * 1.4426950408889634f;
+  return launch_attention(q, k, v, out, D, dtype, prm, reinterpret_cast<cudaStream_t>(stream));
+}

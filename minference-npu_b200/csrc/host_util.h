@@ -1,0 +1,58 @@
+// Host-side helpers: TMA tensor-map construction for BNSD views.
+#pragma once
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/minference_b200.h"
+
+namespace mib200 {
+
+inline size_t align_up(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// cuTensorMapEncodeTiled is fetched through the runtime's driver entry point
+// so the library does not link libcuda directly.
+inline PFN_cuTensorMapEncodeTiled_v12000 get_encode_tiled() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult qres;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qres) ==
+            cudaSuccess &&
+        qres == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 4-D map over a [B, H, S, D] view of 16-bit elements with a box of
+// box_d x box_s elements (box_d * 2 == 64 bytes, 64-byte swizzle).
+// Rows beyond S read as zeros.
+inline int make_bnsd_map(CUtensorMap* map, const mi_tensor4& t, int64_t B, int64_t H, int64_t S,
+                         int64_t D, int box_d, int box_s) {
+  auto enc = get_encode_tiled();
+  if (!enc) return MI_ERR_LAUNCH;
+  if (t.stride_d != 1) return MI_ERR_ALIGN;
+  if (reinterpret_cast<uintptr_t>(t.ptr) & 15) return MI_ERR_ALIGN;
+  const int64_t es = 2;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  int64_t st[3] = {t.stride_s * es, t.stride_h * es, t.stride_b * es};
+  cuuint64_t strides[3];
+  int64_t span = D * es;  // bytes covered by the inner dimensions so far
+  for (int i = 0; i < 3; ++i) {
+    if (dims[i + 1] == 1) st[i] = ((span + 15) / 16) * 16;  // stride of a size-1 dim is unused
+    if (st[i] <= 0 || st[i] % 16) return MI_ERR_ALIGN;
+    strides[i] = (cuuint64_t)st[i];
+    const int64_t ext = st[i] * (int64_t)dims[i + 1];
+    if (ext > span) span = ext;
+  }
+  cuuint32_t box[4] = {(cuuint32_t)box_d, (cuuint32_t)box_s, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, t.ptr, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MI_OK : MI_ERR_ALIGN;
+}
+
+}  // namespace mib200

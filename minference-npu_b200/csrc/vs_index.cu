@@ -1,0 +1,472 @@
+// vertical_and_slash pattern: index estimation (last-64-query softmax,
+// column and diagonal sums, two top-k) and the attention plan built from the
+// direct-mask semantics.
+//
+// Reference semantics:
+//   minference/modules/minference_forward.py:124-167
+//     qk = bf16(q[-64:] @ k^T) / sqrt(D) (rounded to the input dtype again),
+//     last 64x64 causal mask, softmax in fp32, vertical = column sums,
+//     slash = anti-diagonal sums (sum_all_diagonal_matrix), columns 0..29 and
+//     the 100 most local diagonals forced in, two topk, v_idx ascending,
+//     s_idx = S-1-diag descending.
+//   minference/ops/vertical_slash_kernel_npu.py:255-369 (_build_vs_mask_direct)
+//     query block bq, end_m = 64(bq+1): every slash s < end_m keeps keys
+//     [re-64, re) with re = min(max(end_m - s, 64), S); vertical columns are
+//     visible to every row; AND causal.
+//
+// Determinism: every floating-point reduction below has a fixed order and the
+// exponential is an explicit Cody-Waite + degree-7 Taylor evaluation built
+// from IEEE fma/mul/add only, so results are reproducible bit for bit by the
+// C restatement used as the test oracle.
+#include "attention.cuh"
+#include "host_util.h"
+#include "topk.cuh"
+
+namespace mib200 {
+
+// exp(y) for y <= 0 (y < -87 -> 0).  Cody & Waite argument reduction with the
+// classic two-part ln2 split, then the Taylor polynomial of e^r to degree 7
+// (|r| <= ln2/2, truncation error < 6e-9 relative).
+__device__ __forceinline__ float det_exp(float y) {
+  if (!(y >= -87.0f)) return 0.0f;
+  const float n = rintf(__fmul_rn(y, 1.44269504088896341f));
+  float r = __fmaf_rn(-n, 0.693145751953125f, y);
+  r = __fmaf_rn(-n, 1.428606765330187045e-06f, r);
+  float p = 1.0f / 5040.0f;
+  p = __fmaf_rn(p, r, 1.0f / 720.0f);
+  p = __fmaf_rn(p, r, 1.0f / 120.0f);
+  p = __fmaf_rn(p, r, 1.0f / 24.0f);
+  p = __fmaf_rn(p, r, 1.0f / 6.0f);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  const float scale = __int_as_float(((int)n + 127) << 23);
+  return __fmul_rn(p, scale);
+}
+
+constexpr double kFixScale = 17592186044416.0;  // 2^44: row sums in 64-bit fixed point
+
+// ---------------------------------------------------------------------------
+// K3a: logits x[i][c] for the last LQ queries, rounded like the reference:
+// round_dt(round_dt(dot) / sqrt_d); masked (c > S-LQ+i) entries are -inf.
+// Stored as the input dtype's bits: x: [BH][LQ][S] uint16.
+// Grid (ceil(S/128), H, B), 128 threads: thread = one key column.
+// ---------------------------------------------------------------------------
+template <typename DT, int D>
+__global__ void __launch_bounds__(128) vs_logits_kernel(mi_tensor4 q, mi_tensor4 k, int H, int S,
+                                                        int LQ, float sqrt_d, uint16_t* x) {
+  __shared__ float qs[64][D];
+  const int h = blockIdx.y, b = blockIdx.z, bh = b * H + h;
+  const uint16_t* qb = reinterpret_cast<const uint16_t*>(q.ptr) + (long long)b * q.stride_b +
+                       (long long)h * q.stride_h;
+  for (int e = threadIdx.x; e < LQ * D; e += blockDim.x) {
+    const int i = e / D, d = e % D;
+    qs[i][d] = DType<DT>::to_f(qb[(long long)(S - LQ + i) * q.stride_s + d]);
+  }
+  __syncthreads();
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= S) return;
+  const uint16_t* kr = reinterpret_cast<const uint16_t*>(k.ptr) + (long long)b * k.stride_b +
+                       (long long)h * k.stride_h + (long long)c * k.stride_s;
+  float kv[D];
+#pragma unroll
+  for (int d = 0; d < D; d += 8) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(kr + d);
+    const uint16_t* hv = reinterpret_cast<const uint16_t*>(&raw);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) kv[d + u] = DType<DT>::to_f(hv[u]);
+  }
+  uint16_t* xo = x + (long long)bh * LQ * S + c;
+  for (int i = 0; i < LQ; ++i) {
+    uint16_t bits;
+    if (c > S - LQ + i) {
+      bits = DType<DT>::kBF16 ? (uint16_t)0xFF80 : (uint16_t)0xFC00;  // -inf
+    } else {
+      float acc = 0.f;
+#pragma unroll
+      for (int d = 0; d < D; ++d) acc = __fmaf_rn(qs[i][d], kv[d], acc);
+      const float r1 = DType<DT>::round(acc);
+      const float r2 = DType<DT>::round(__fdiv_rn(r1, sqrt_d));
+      if (DType<DT>::kBF16) {
+        bits = (uint16_t)(__float_as_uint(r2) >> 16);
+      } else {
+        bits = __half_as_ushort(__float2half_rn(r2));
+      }
+    }
+    xo[(long long)i * S] = bits;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// K3b: per-row max and sum of exp(x - max) (64-bit fixed point, so the sum is
+// independent of the reduction order).  Grid (LQ, H, B), 1024 threads.
+// stats: [BH][LQ] {m, l}.
+// ---------------------------------------------------------------------------
+template <typename DT>
+__global__ void __launch_bounds__(1024) vs_rowstats_kernel(const uint16_t* x, int H, int S,
+                                                           int LQ, float2* stats) {
+  __shared__ float red_m[32];
+  __shared__ unsigned long long red_s[32];
+  const int i = blockIdx.x, h = blockIdx.y, b = blockIdx.z, bh = b * H + h;
+  const uint16_t* xr = x + ((long long)bh * LQ + i) * S;
+  float m = -INFINITY;
+  for (int c = threadIdx.x; c < S; c += blockDim.x) m = fmaxf(m, DType<DT>::to_f(xr[c]));
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red_m[threadIdx.x >> 5] = m;
+  __syncthreads();
+  m = red_m[0];
+  for (int w = 1; w < 32; ++w) m = fmaxf(m, red_m[w]);
+  unsigned long long s = 0;
+  for (int c = threadIdx.x; c < S; c += blockDim.x) {
+    const float e = det_exp(__fsub_rn(DType<DT>::to_f(xr[c]), m));
+    s += (unsigned long long)__float2ll_rz((float)(e * (float)kFixScale));
+  }
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) red_s[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long tot = 0;
+    for (int w = 0; w < 32; ++w) tot += red_s[w];
+    stats[(long long)bh * LQ + i] = make_float2(m, (float)((double)tot / kFixScale));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// K3c: p[i][c] = det_exp(x - m_i) / l_i;  vertical[c] = sum_i p[i][c];
+// slash[t] = sum_i p[i][t + 1 + i - LQ] (columns outside [0,S) add nothing),
+// both summed in row order.  Forced entries (c < 30, t >= S-100) get +inf.
+// Output: order-preserving keys vkeys/skeys [BH][S].
+// ---------------------------------------------------------------------------
+template <typename DT>
+__global__ void __launch_bounds__(256) vs_sums_kernel(const uint16_t* x, const float2* stats,
+                                                      int H, int S, int LQ, uint32_t* vkeys,
+                                                      uint32_t* skeys) {
+  __shared__ float2 st[64];
+  const int h = blockIdx.y, b = blockIdx.z, bh = b * H + h;
+  if (threadIdx.x < LQ) st[threadIdx.x] = stats[(long long)bh * LQ + threadIdx.x];
+  __syncthreads();
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= S) return;
+  const uint16_t* xb = x + (long long)bh * LQ * S;
+  float vs = 0.f, ds = 0.f;
+  for (int i = 0; i < LQ; ++i) {
+    const float pv = __fdiv_rn(det_exp(__fsub_rn(DType<DT>::to_f(xb[(long long)i * S + c]), st[i].x)), st[i].y);
+    vs = __fadd_rn(vs, pv);
+    const int col = c + 1 + i - LQ;
+    if (col >= 0 && col < S) {
+      const float pd = __fdiv_rn(det_exp(__fsub_rn(DType<DT>::to_f(xb[(long long)i * S + col]), st[i].x)), st[i].y);
+      ds = __fadd_rn(ds, pd);
+    }
+  }
+  if (c < 30) vs = INFINITY;
+  if (c >= S - 100) ds = INFINITY;
+  vkeys[(long long)bh * S + c] = float_to_ordered(vs);
+  skeys[(long long)bh * S + c] = float_to_ordered(ds);
+}
+
+// K3d: the two top-k selections.  Grid (H, B, 2), 1024 threads.
+constexpr int kVsSelThreads = 1024;
+__global__ void __launch_bounds__(kVsSelThreads) vs_select_kernel(const uint32_t* vkeys,
+                                                                  const uint32_t* skeys, int H,
+                                                                  int S, int nv, int ns,
+                                                                  int32_t* v_idx, int32_t* s_idx) {
+  __shared__ TopkSmem<kVsSelThreads> tsm;
+  const int h = blockIdx.x, b = blockIdx.y, bh = b * H + h;
+  if (blockIdx.z == 0) {
+    int32_t* dst = v_idx + (long long)bh * nv;
+    block_topk<kVsSelThreads>(vkeys + (long long)bh * S, S, nv, tsm,
+                              [&](int pos, int idx) { dst[pos] = idx; });
+  } else {
+    int32_t* dst = s_idx + (long long)bh * ns;
+    block_topk<kVsSelThreads>(skeys + (long long)bh * S, S, ns, tsm,
+                              [&](int pos, int idx) { dst[pos] = S - 1 - idx; });
+  }
+}
+
+// ---------------------------------------------------------------------------
+// K4a: per-head tables for the direct mask.
+//   P[x]      number of distinct slashes s < x (x = 0..S)
+//   vmask[kb] vertical columns of key block kb (64-bit)
+//   smask[D]  for query block bq and key block kb = bq - D (not the ragged
+//             last query block): key 64*kb + c is covered by a slash iff some
+//             s lies in [D*64 - c, D*64 - c + 63]
+//   clow[bq]  some slash s in (64*bq, 64*bq + 64) (range clamped to [0,64))
+// Grid (H, B), 1024 threads.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ bool any_slash(const int* P, long long lo, long long hi, int S) {
+  if (lo < 0) lo = 0;
+  if (hi > S - 1) hi = S - 1;
+  if (hi < lo) return false;
+  return P[hi + 1] - P[lo] > 0;
+}
+
+__global__ void __launch_bounds__(1024) vs_tables_kernel(const int32_t* v_idx, int nv,
+                                                         const int32_t* s_idx, int ns, int H,
+                                                         int S, int nb, int* Pall,
+                                                         unsigned long long* vmask_all,
+                                                         uint32_t* smask_all, int* clow_all) {
+  __shared__ int warp_tot[32];
+  const int h = blockIdx.x, b = blockIdx.y, bh = b * H + h;
+  int* P = Pall + (long long)bh * (S + 1);
+  unsigned long long* vmask = vmask_all + (long long)bh * nb;
+  uint32_t* smask = smask_all + (long long)bh * nb * 2;
+  int* clow = clow_all + (long long)bh * nb;
+  for (int i = threadIdx.x; i <= S; i += blockDim.x) P[i] = 0;
+  for (int i = threadIdx.x; i < nb; i += blockDim.x) vmask[i] = 0ull;
+  __syncthreads();
+  for (int i = threadIdx.x; i < ns; i += blockDim.x) {
+    const int s = s_idx[(long long)bh * ns + i];
+    if (s >= 0 && s < S) P[s] = 1;
+  }
+  for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+    int c = v_idx[(long long)bh * nv + i];
+    c = c < 0 ? 0 : (c > S - 1 ? S - 1 : c);
+    atomicOr(&vmask[c >> 6], 1ull << (c & 63));
+  }
+  __syncthreads();
+  // exclusive scan of P[0..S] in place
+  const int n = S + 1;
+  const int ept = (n + blockDim.x - 1) / blockDim.x;
+  const int beg = min(n, (int)threadIdx.x * ept), end = min(n, beg + ept);
+  int local = 0;
+  for (int i = beg; i < end; ++i) local += P[i];
+  int tot;
+  const int pre = block_exclusive_scan<1024>(local, warp_tot, &tot);
+  int run = pre;
+  for (int i = beg; i < end; ++i) {
+    const int vv = P[i];
+    P[i] = run;
+    run += vv;
+  }
+  __syncthreads();
+  for (int base = 0; base < nb * 64; base += blockDim.x) {
+    const int idx = base + threadIdx.x;
+    bool bit = false;
+    if (idx < nb * 64) {
+      const long long Dl = idx >> 6, c = idx & 63;
+      const long long d = Dl * 64 - c;
+      bit = any_slash(P, d, d + 63, S);
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, bit);
+    if ((threadIdx.x & 31) == 0 && idx < nb * 64) smask[idx >> 5] = bal;
+  }
+  for (int bq = threadIdx.x; bq < nb; bq += blockDim.x)
+    clow[bq] = any_slash(P, (long long)bq * 64 + 1, (long long)bq * 64 + 63, S) ? 1 : 0;
+}
+
+// Mask of key block kb for query block bq (rows [64bq, 64bq+64)), before the
+// per-element causal / key < S test applied by the attention kernel.
+__device__ __forceinline__ uint64_t vs_block_mask(int bq, int kb, int S, int nb, const int* P,
+                                                  const unsigned long long* vmask,
+                                                  const uint32_t* smask, const int* clow) {
+  uint64_t m = vmask[kb];
+  if (kb == 0 && clow[bq]) m = ~0ull;
+  const bool ragged_last = (bq == nb - 1) && (S % 64 != 0);
+  if (!ragged_last) {
+    const int Dl = bq - kb;
+    m |= (uint64_t)smask[2 * Dl] | ((uint64_t)smask[2 * Dl + 1] << 32);
+  } else {
+    const long long end_m = (long long)nb * 64;
+    const long long lo_bound = end_m - S;  // slashes below this are clamped to [S-64, S)
+    const bool high = any_slash(P, 0, lo_bound - 1, S);
+    for (int c = 0; c < 64; ++c) {
+      const long long j = (long long)kb * 64 + c;
+      if (j >= S) break;
+      const long long d = (long long)bq * 64 - j;
+      long long lo = d > lo_bound ? d : lo_bound;
+      bool bit = any_slash(P, lo, d + 63, S);
+      if (high && j >= (long long)S - 64) bit = true;
+      if (bit) m |= 1ull << c;
+    }
+  }
+  return m;
+}
+
+// K4b: plan.  One warp per 128-row query tile; entries in ascending kb.
+__global__ void __launch_bounds__(128) vs_plan_kernel(int H, int S, int nb, int T,
+                                                      const int* Pall,
+                                                      const unsigned long long* vmask_all,
+                                                      const uint32_t* smask_all,
+                                                      const int* clow_all, long long cap,
+                                                      long long head_stride, PlanEntry* plan,
+                                                      int* plan_count) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 4 + w;
+  const int h = blockIdx.y, b = blockIdx.z, bh = b * H + h;
+  if (t >= T) return;
+  const int* P = Pall + (long long)bh * (S + 1);
+  const unsigned long long* vmask = vmask_all + (long long)bh * nb;
+  const uint32_t* smask = smask_all + (long long)bh * nb * 2;
+  const int* clow = clow_all + (long long)bh * nb;
+  const int bq0 = 2 * t, bq1 = 2 * t + 1;
+  const int hi = min(bq1, nb - 1);
+  PlanEntry* out = plan + (long long)bh * head_stride + plan_offset(t, cap);
+  int count = 0;
+  for (int base = 0; base <= hi; base += 32) {
+    const int kb = base + lane;
+    uint64_t m0 = 0, m1 = 0;
+    if (kb <= hi) {
+      if (bq0 < nb && kb <= bq0) m0 = vs_block_mask(bq0, kb, S, nb, P, vmask, smask, clow);
+      if (bq1 < nb && kb <= bq1) m1 = vs_block_mask(bq1, kb, S, nb, P, vmask, smask, clow);
+    }
+    const bool keep = (m0 | m1) != 0ull;
+    const unsigned bal = __ballot_sync(0xffffffffu, keep);
+    if (keep) {
+      PlanEntry e;
+      e.kb = kb;
+      e.pad = 0;
+      e.m0 = m0;
+      e.m1 = m1;
+      out[count + __popc(bal & ((1u << lane) - 1u))] = e;
+    }
+    count += __popc(bal);
+  }
+  if (lane == 0) plan_count[(long long)bh * T + t] = count;
+}
+
+
+int launch_attention(const mi_tensor4& q, const mi_tensor4& k, const mi_tensor4& v,
+                     const mi_tensor4& out, int64_t D, int dtype, AttnParams prm,
+                     cudaStream_t stream);
+
+}  // namespace mib200
+
+using namespace mib200;
+
+// ---------------------------------------------------------------------------
+// Estimation entry point
+// ---------------------------------------------------------------------------
+extern "C" size_t mi_vs_estimate_workspace_size(int64_t B, int64_t H, int64_t S) {
+  const int64_t LQ = S < 64 ? S : 64;
+  return align_up(2ull * B * H * LQ * S) + align_up(sizeof(float2) * B * H * LQ) +
+         2 * align_up(4ull * B * H * S);
+}
+
+template <typename DT, int D>
+static void launch_vs_logits(const mi_tensor4& q, const mi_tensor4& k, int64_t B, int64_t H,
+                             int64_t S, int LQ, float sqrt_d, uint16_t* x, cudaStream_t st) {
+  dim3 g((unsigned)((S + 127) / 128), (unsigned)H, (unsigned)B);
+  vs_logits_kernel<DT, D><<<g, 128, 0, st>>>(q, k, (int)H, (int)S, LQ, sqrt_d, x);
+}
+
+extern "C" int mi_vs_estimate(mi_tensor4 q, mi_tensor4 k, int64_t B, int64_t H, int64_t S,
+                              int64_t D, int dtype, int64_t vertical_size, int64_t slash_size,
+                              float logit_scale, int32_t* v_idx, int32_t* s_idx, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  if (dtype != MI_F16 && dtype != MI_BF16) return MI_ERR_DTYPE;
+  if (D != 64 && D != 96 && D != 128) return MI_ERR_SHAPE;
+  if (B < 0 || H < 0 || S < 0 || S > (1 << 24)) return MI_ERR_SHAPE;
+  if (vertical_size < 1 || vertical_size > S || slash_size < 1 || slash_size > S)
+    return MI_ERR_SHAPE;
+  if (q.stride_d != 1 || k.stride_d != 1 || (k.stride_s % 8) || (reinterpret_cast<uintptr_t>(k.ptr) & 15))
+    return MI_ERR_ALIGN;
+  if (B == 0 || H == 0 || S == 0) return MI_OK;
+  if (!workspace || workspace_bytes < mi_vs_estimate_workspace_size(B, H, S)) return MI_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int LQ = (int)(S < 64 ? S : 64);
+  char* w = reinterpret_cast<char*>(workspace);
+  uint16_t* x = reinterpret_cast<uint16_t*>(w);
+  w += align_up(2ull * B * H * LQ * S);
+  float2* stats = reinterpret_cast<float2*>(w);
+  w += align_up(sizeof(float2) * B * H * LQ);
+  uint32_t* vkeys = reinterpret_cast<uint32_t*>(w);
+  w += align_up(4ull * B * H * S);
+  uint32_t* skeys = reinterpret_cast<uint32_t*>(w);
+  // The reference divides by sqrt(D); logit_scale is 1/sqrt(D), so divide by its inverse.
+  const float sqrt_d = 1.0f / logit_scale;
+  const bool bf = dtype == MI_BF16;
+#define VS_LOG(DD)                                                                              \
+  if (D == DD) {                                                                                \
+    if (bf) launch_vs_logits<__nv_bfloat16, DD>(q, k, B, H, S, LQ, sqrt_d, x, st);              \
+    else launch_vs_logits<__half, DD>(q, k, B, H, S, LQ, sqrt_d, x, st);                        \
+  }
+  VS_LOG(64) VS_LOG(96) VS_LOG(128)
+#undef VS_LOG
+  dim3 g2((unsigned)LQ, (unsigned)H, (unsigned)B);
+  dim3 g3((unsigned)((S + 255) / 256), (unsigned)H, (unsigned)B);
+  if (bf) {
+    vs_rowstats_kernel<__nv_bfloat16><<<g2, 1024, 0, st>>>(x, (int)H, (int)S, LQ, stats);
+    vs_sums_kernel<__nv_bfloat16><<<g3, 256, 0, st>>>(x, stats, (int)H, (int)S, LQ, vkeys, skeys);
+  } else {
+    vs_rowstats_kernel<__half><<<g2, 1024, 0, st>>>(x, (int)H, (int)S, LQ, stats);
+    vs_sums_kernel<__half><<<g3, 256, 0, st>>>(x, stats, (int)H, (int)S, LQ, vkeys, skeys);
+  }
+  dim3 g4((unsigned)H, (unsigned)B, 2);
+  vs_select_kernel<<<g4, kVsSelThreads, 0, st>>>(vkeys, skeys, (int)H, (int)S, (int)vertical_size,
+                                                 (int)slash_size, v_idx, s_idx);
+  return cudaGetLastError() == cudaSuccess ? MI_OK : MI_ERR_LAUNCH;
+}
+
+// ---------------------------------------------------------------------------
+// Sparse attention entry point
+// ---------------------------------------------------------------------------
+struct VsWs {
+  int* P;
+  unsigned long long* vmask;
+  uint32_t* smask;
+  int* clow;
+  PlanEntry* plan;
+  int* count;
+  size_t bytes;
+};
+
+static VsWs vs_ws_layout(void* base, int64_t B, int64_t H, int64_t S) {
+  const int64_t nb = (S + 63) / 64, T = (S + 127) / 128;
+  const int64_t cap = 2 * T;
+  VsWs w{};
+  char* p = reinterpret_cast<char*>(base);
+  size_t off = 0;
+  auto take = [&](size_t n) { char* r = p ? p + off : nullptr; off += align_up(n); return r; };
+  w.P = reinterpret_cast<int*>(take(4ull * B * H * (S + 1)));
+  w.vmask = reinterpret_cast<unsigned long long*>(take(8ull * B * H * nb));
+  w.smask = reinterpret_cast<uint32_t*>(take(8ull * B * H * nb));
+  w.clow = reinterpret_cast<int*>(take(4ull * B * H * nb));
+  w.plan = reinterpret_cast<PlanEntry*>(take(sizeof(PlanEntry) * B * H * plan_offset(T, cap)));
+  w.count = reinterpret_cast<int*>(take(4ull * B * H * T));
+  w.bytes = off;
+  return w;
+}
+
+extern "C" size_t mi_vs_sparse_fwd_workspace_size(int64_t B, int64_t H, int64_t S) {
+  return vs_ws_layout(nullptr, B, H, S).bytes;
+}
+
+extern "C" int mi_vs_sparse_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor4 out,
+                                int64_t B, int64_t H, int64_t S, int64_t D, int dtype,
+                                const int32_t* v_idx, int64_t nv, const int32_t* s_idx,
+                                int64_t ns, float softmax_scale, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  if (dtype != MI_F16 && dtype != MI_BF16) return MI_ERR_DTYPE;
+  if (D != 64 && D != 96 && D != 128) return MI_ERR_SHAPE;
+  if (B < 0 || H < 0 || S < 0 || nv < 0 || ns < 0 || S > (1 << 24)) return MI_ERR_SHAPE;
+  if (B > 65535 || H > 65535) return MI_ERR_SHAPE;
+  if (B == 0 || H == 0 || S == 0) return MI_OK;
+  const VsWs w = vs_ws_layout(workspace, B, H, S);
+  if (!workspace || workspace_bytes < w.bytes) return MI_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t nb = (S + 63) / 64, T = (S + 127) / 128;
+  const int64_t cap = 2 * T;
+  const int64_t head_stride = plan_offset(T, cap);
+  vs_tables_kernel<<<dim3((unsigned)H, (unsigned)B), 1024, 0, st>>>(
+      v_idx, (int)nv, s_idx, (int)ns, (int)H, (int)S, (int)nb, w.P, w.vmask, w.smask, w.clow);
+  dim3 g((unsigned)((T + 3) / 4), (unsigned)H, (unsigned)B);
+  vs_plan_kernel<<<g, 128, 0, st>>>((int)H, (int)S, (int)nb, (int)T, w.P, w.vmask, w.smask,
+                                    w.clow, cap, head_stride, w.plan, w.count);
+  if (cudaGetLastError() != cudaSuccess) return MI_ERR_LAUNCH;
+  AttnParams prm{};
+  prm.B = (int)B;
+  prm.H = (int)H;
+  prm.Sq = (int)S;
+  prm.Sk = (int)S;
+  prm.q_off = 0;
+  prm.T = (int)T;
+  prm.mode = 1;
+  prm.n_init = 0;
+  prm.n_local = S + 1;
+  prm.scale_log2 = softmax_scale * 1.4426950408889634f;
+  prm.plan = w.plan;
+  prm.plan_count = w.count;
+  prm.plan_cap = cap;
+  prm.plan_head_stride = head_stride;
+  return launch_attention(q, k, v, out, D, dtype, prm, st);
+}

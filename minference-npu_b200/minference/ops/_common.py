@@ -1,0 +1,87 @@
+"""Shared helpers of the op wrappers: head-dim handling and softmax scale."""
+
+from __future__ import annotations
+
+import math
+import os
+
+import torch
+import torch.nn.functional as F
+
+from .. import _native
+
+# head dims the reference's NPU kernels accept; other dims are zero-padded to
+# the next one of these and the softmax scale is taken from the padded dim
+# (block_sparse_kernel_npu.py:651-656 then :340, streaming_kernel_npu.py:377-381
+# then :114, vertical_slash_kernel_npu.py:568-573 then :409).
+_REF_ALLOWED_HEAD_DIMS = (16, 32, 64, 128, 256, 512)
+# head dims the sm_100a kernels are compiled for
+_KERNEL_HEAD_DIMS = (64, 96, 128)
+
+TRUE_SCALE_ENV = "MINFERENCE_TRUE_SCALE"
+
+
+def reference_padded_dim(d: int) -> int:
+    for c in _REF_ALLOWED_HEAD_DIMS:
+        if c >= d:
+            return c
+    raise ValueError(f"head_dim={d} exceeds the largest supported value {_REF_ALLOWED_HEAD_DIMS[-1]}")
+
+
+def default_softmax_scale(d: int) -> float:
+    """Reference-compatible scale 1/sqrt(padded D); 1/sqrt(D) when MINFERENCE_TRUE_SCALE=1."""
+    if os.environ.get(TRUE_SCALE_ENV, "").strip().lower() in {"1", "true", "yes", "on"}:
+        return 1.0 / math.sqrt(d)
+    return 1.0 / math.sqrt(reference_padded_dim(d))
+
+
+def kernel_dim(d: int) -> int:
+    for c in _KERNEL_HEAD_DIMS:
+        if c >= d:
+            return c
+    raise NotImplementedError(f"head_dim={d} > 128 is not supported by the sm_100a kernels")
+
+
+def prepare(x: torch.Tensor, dk: int) -> torch.Tensor:
+    """Zero-pad the head dim to dk and make rows usable by TMA (unit D stride,
+    16-byte aligned row starts)."""
+    if x.shape[-1] != dk:
+        x = F.pad(x, (0, dk - x.shape[-1]))
+    s = x.stride()
+    if (
+        s[-1] != 1
+        or (s[0] * 2) % 16
+        or (s[1] * 2) % 16
+        or (s[2] * 2) % 16
+        or x.data_ptr() % 16
+    ):
+        x = x.contiguous()
+    return x
+
+
+def check_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
+    assert q.dim() == 4, f"q must be 4D [B,H,S,D], got {q.dim()}D"
+    assert (
+        q.shape[0] == k.shape[0] and q.shape[1] == k.shape[1] and q.shape[-1] == k.shape[-1]
+    ), f"q/k B/H/D mismatch; q={tuple(q.shape)} k={tuple(k.shape)}"
+    assert k.shape == v.shape, f"k/v shape mismatch; k={tuple(k.shape)} v={tuple(v.shape)}"
+    _native.require_cuda(q, k, v)
+    if not (q.dtype == k.dtype == v.dtype):
+        raise TypeError(f"q/k/v dtypes differ: {q.dtype}, {k.dtype}, {v.dtype}")
+    _native.dtype_code(q)
+
+
+def output(out: torch.Tensor | None, shape: tuple, like: torch.Tensor) -> torch.Tensor:
+    """The output tensor: a new one, or a caller-provided [B,H,S,D] view (any
+    strides with unit D stride and 16-byte aligned rows) written in place."""
+    if out is None:
+        return torch.empty(shape, dtype=like.dtype, device=like.device)
+    if tuple(out.shape) != tuple(shape) or out.dtype != like.dtype or out.device != like.device:
+        raise ValueError(
+            f"out must be {tuple(shape)} {like.dtype} on {like.device}; got "
+            f"{tuple(out.shape)} {out.dtype} on {out.device}"
+        )
+    s = out.stride()
+    if s[-1] != 1 or (s[0] * 2) % 16 or (s[1] * 2) % 16 or (s[2] * 2) % 16 or out.data_ptr() % 16:
+        raise ValueError("out needs unit D stride and 16-byte aligned rows")
+    return out

@@ -1,0 +1,84 @@
+"""vertical_and_slash pattern: top-k key columns plus top-k diagonals.
+
+Drop-ins for the estimator ``_vertical_and_slash_kernel`` (MInference-NPU
+minference/modules/minference_forward.py:140-167) and the attention
+``vertical_slash_sparse_attention`` (minference/ops/vertical_slash_kernel_npu.py:518).
+The attention follows the reference's direct mask (:255-369) at every
+sequence length; the reference's own entry point switches to dense causal
+attention above 16384 tokens (:582-592), which is not reproduced here.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import _native
+from ._common import check_qkv, default_softmax_scale, kernel_dim, prepare
+from ._common import output as _common_out
+
+__all__ = ["vertical_slash_sparse_attention", "vertical_and_slash_estimate", "vertical_and_slash"]
+
+LAST_Q = 64
+
+
+def vertical_and_slash_estimate(q: torch.Tensor, k: torch.Tensor, vertical_size: int,
+                                slash_size: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """(v_idx int32 [B,H,nv] ascending, s_idx int32 [B,H,ns] descending) from the last 64 queries."""
+    _native.require_cuda(q, k)
+    B, H, S, D = q.shape
+    nv = min(S, max(int(vertical_size), 30))
+    ns = min(S, max(int(slash_size), 50))
+    dk = kernel_dim(D)
+    logit_scale = 1.0 / math.sqrt(D)  # the estimator uses the unpadded head dim
+    qp, kp = prepare(q, dk), prepare(k, dk)
+    v_idx = torch.empty((B, H, nv), dtype=torch.int32, device=q.device)
+    s_idx = torch.empty((B, H, ns), dtype=torch.int32, device=q.device)
+    ws = _native.workspace(_native.lib().mi_vs_estimate_workspace_size(B, H, S), q.device)
+    with torch.cuda.device(q.device):
+        rc = _native.lib().mi_vs_estimate(
+            _native.t4(qp), _native.t4(kp), B, H, S, dk, _native.dtype_code(q), nv, ns,
+            logit_scale, v_idx.data_ptr(), s_idx.data_ptr(), ws.data_ptr(), ws.numel(),
+            _native.stream_ptr(q.device),
+        )
+    _native.check(rc, "mi_vs_estimate")
+    return v_idx, s_idx
+
+
+def vertical_slash_sparse_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                                    v_idx: torch.Tensor, s_idx: torch.Tensor,
+                                    block_size_M: int = 64, block_size_N: int = 64,
+                                    softmax_scale: float | None = None, *,
+                                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """Vertical-slash causal attention; same signature as the reference op."""
+    check_qkv(query, key, value)
+    if block_size_M != 64 or block_size_N != 64:
+        raise NotImplementedError("block_size_M/N must be 64")
+    B, H, S, D = query.shape
+    assert key.shape[2] == S, (
+        f"vertical_slash_sparse_attention supports full prefill only (S_q == S_k); "
+        f"got S_q={S}, S_k={key.shape[2]}"
+    )
+    scale = default_softmax_scale(D) if softmax_scale is None else float(softmax_scale)
+    dk = kernel_dim(D)
+    vi = v_idx.to(device=query.device, dtype=torch.int32).reshape(B, H, -1).contiguous()
+    si = s_idx.to(device=query.device, dtype=torch.int32).reshape(B, H, -1).contiguous()
+    qp, kp, vp = prepare(query, dk), prepare(key, dk), prepare(value, dk)
+    out = _common_out(out, (B, H, S, dk), query)
+    ws = _native.workspace(_native.lib().mi_vs_sparse_fwd_workspace_size(B, H, S), query.device)
+    with torch.cuda.device(query.device):
+        rc = _native.lib().mi_vs_sparse_fwd(
+            _native.t4(qp), _native.t4(kp), _native.t4(vp), _native.t4(out), B, H, S, dk,
+            _native.dtype_code(query), vi.data_ptr(), vi.shape[-1], si.data_ptr(), si.shape[-1],
+            scale, ws.data_ptr(), ws.numel(), _native.stream_ptr(query.device),
+        )
+    _native.check(rc, "mi_vs_sparse_fwd")
+    return out[..., :D] if dk != D else out
+
+
+def vertical_and_slash(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, vertical_size: int,
+                       slash_size: int, *, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Estimate indices from the last 64 queries, then run the sparse attention."""
+    v_idx, s_idx = vertical_and_slash_estimate(q, k, vertical_size, slash_size)
+    return vertical_slash_sparse_attention(q, k, v, v_idx, s_idx, out=out)

@@ -1,0 +1,223 @@
+"""Generate golden vectors from the reference implementation itself.
+
+Run in a container that has the reference checkout (default
+/root/reference/MInference-NPU, override with MINFERENCE_REF):
+
+    python tests/golden/make_golden.py
+
+It imports the reference's own CPU code paths (the NPU paths are not
+importable without torch_npu) and stores seeded inputs together with the
+reference outputs as compressed .npz files next to this script.  The tests
+(tests/test_oracle_golden.py, tests/test_gpu_parity.py) only read those
+files; they never import the reference.
+
+Reference functions exercised (paths relative to the project root):
+  ops/block_sparse_kernel_npu.py   _select_block_sparse_topk_indices (:230),
+                                   _build_block_sparse_mask (:266),
+                                   block_sparse_attention (:609)
+  ops/streaming_kernel_npu.py      streaming_forward (:349)
+  modules/minference_forward.py    _vertical_and_slash_kernel (:140)
+  ops/vertical_slash_kernel_npu.py _build_vs_mask_direct (:255),
+                                   _vertical_slash_pytorch_ref (:377)
+"""
+
+from __future__ import annotations
+
+import importlib
+import importlib.util
+import math
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+sys.dont_write_bytecode = True
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF = os.environ.get("MINFERENCE_REF", "/root/reference/MInference-NPU")
+
+
+def _load_ref_package():
+    pkg_dir = os.path.join(REF, "minference")
+    spec = importlib.util.spec_from_file_location(
+        "ref_minference", os.path.join(pkg_dir, "__init__.py"), submodule_search_locations=[pkg_dir]
+    )
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["ref_minference"] = mod
+    spec.loader.exec_module(mod)
+
+    bs = importlib.import_module("ref_minference.ops.block_sparse_kernel_npu")
+    st = importlib.import_module("ref_minference.ops.streaming_kernel_npu")
+    vs = importlib.import_module("ref_minference.ops.vertical_slash_kernel_npu")
+    fw = importlib.import_module("ref_minference.modules.minference_forward")
+    return bs, st, vs, fw
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def gen_qkv(B, H, S, D, dtype, seed, lowrank=0.0, sinks=0):
+    """Q,K,V ~ N(0,1)/sqrt(D); optional rank-4 bias on K and x4 'sink' rows."""
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, H, S, D, generator=g) / math.sqrt(D)
+    k = torch.randn(B, H, S, D, generator=g) / math.sqrt(D)
+    v = torch.randn(B, H, S, D, generator=g) / math.sqrt(D)
+    if lowrank:
+        u = torch.randn(B, H, S, 4, generator=g)
+        w = torch.randn(B, H, 4, D, generator=g) / math.sqrt(4 * D)
+        k = k + lowrank * (u @ w)
+    if sinks:
+        for b in range(B):
+            for h in range(H):
+                pos = torch.randperm(S, generator=g)[:sinks]
+                k[b, h, pos] *= 4.0
+    return q.to(dtype), k.to(dtype), v.to(dtype)
+
+
+def pad128(t):
+    return F.pad(t, (0, 128 - t.shape[-1])) if t.shape[-1] < 128 else t
+
+
+def main() -> None:
+    bs, st, vs, fw = _load_ref_package()
+    torch.set_num_threads(min(8, os.cpu_count() or 1))
+
+    # ---- block_sparse selector ------------------------------------------------
+    sel_cases = [
+        # (S, D, dtype, topk, seed, lowrank)
+        (300, 96, torch.bfloat16, 3, 1, 0.0),
+        (1024, 96, torch.float16, 4, 2, 0.0),
+        (2048, 96, torch.bfloat16, 8, 3, 2.0),
+        (4096, 96, torch.bfloat16, 100, 4, 2.0),
+        (640, 64, torch.bfloat16, 64, 5, 0.0),  # topk > nb: future blocks padded
+    ]
+    out = {}
+    for ci, (S, D, dt, topk, seed, lr) in enumerate(sel_cases):
+        q, k, _ = gen_qkv(1, 2, S, D, dt, seed, lowrank=lr)
+        qp, kp = pad128(q), pad128(k)
+        idx = bs._select_block_sparse_topk_indices(qp, kp, topk, 64)
+        # reference scores (same expressions as :251-260) for tie analysis
+        nb = -(-S // 64)
+        padn = nb * 64 - S
+        qq = F.pad(qp, (0, 0, 0, padn)) if padn else qp
+        kk = F.pad(kp, (0, 0, 0, padn)) if padn else kp
+        qpool = qq.reshape(1, 2, nb, 64, qp.shape[-1]).mean(dim=3).float()
+        kpool = kk.reshape(1, 2, nb, 64, kp.shape[-1]).mean(dim=3).float()
+        scores = torch.matmul(qpool, kpool.transpose(-2, -1)) * (qp.shape[-1] ** -0.5)
+        out[f"c{ci}_q"] = bits(q)
+        out[f"c{ci}_k"] = bits(k)
+        out[f"c{ci}_meta"] = np.array([S, D, int(dt == torch.bfloat16), topk, qp.shape[-1]])
+        out[f"c{ci}_idx"] = idx.numpy()
+        out[f"c{ci}_scores"] = scores.numpy()
+    out["n_cases"] = np.array(len(sel_cases))
+    np.savez_compressed(os.path.join(HERE, "block_select.npz"), **out)
+
+    # ---- block_sparse attention (op) + token mask --------------------------------
+    att_cases = [
+        (256, 96, torch.bfloat16, 2, 11),
+        (300, 96, torch.float16, 3, 12),
+        (512, 64, torch.bfloat16, 100, 13),  # full topk == dense causal
+    ]
+    out = {}
+    for ci, (S, D, dt, topk, seed) in enumerate(att_cases):
+        q, k, v = gen_qkv(1, 2, S, D, dt, seed, lowrank=2.0)
+        o = bs.block_sparse_attention(q, k, v, topk)
+        mask = bs._build_block_sparse_mask(pad128(q), pad128(k), topk, 64)
+        out[f"c{ci}_q"], out[f"c{ci}_k"], out[f"c{ci}_v"] = bits(q), bits(k), bits(v)
+        out[f"c{ci}_meta"] = np.array([S, D, int(dt == torch.bfloat16), topk])
+        out[f"c{ci}_out"] = bits(o)
+        out[f"c{ci}_visible"] = (~mask).numpy()
+    out["n_cases"] = np.array(len(att_cases))
+    np.savez_compressed(os.path.join(HERE, "block_sparse_attn.npz"), **out)
+
+    # ---- stream_llm -------------------------------------------------------------
+    stream_cases = [
+        # (n_init, n_local, s_q, s_k, D, dtype, seed)
+        (4, 8, 9, 9, 96, torch.float16, 21),
+        (0, 16, 32, 64, 96, torch.float16, 22),
+        (128, 512, 512, 1024, 96, torch.float16, 23),
+        (400, 128, 128, 512, 64, torch.bfloat16, 24),
+        (64, 512, 256, 256, 96, torch.bfloat16, 25),  # short circuit: dense causal
+        (128, 256, 700, 700, 96, torch.float16, 26),
+    ]
+    out = {}
+    for ci, (ni, nl, sq, sk, D, dt, seed) in enumerate(stream_cases):
+        g = torch.Generator().manual_seed(seed)
+        q = (torch.randn(1, 2, sq, D, generator=g) / math.sqrt(D)).to(dt)
+        k = (torch.randn(1, 2, sk, D, generator=g) / math.sqrt(D)).to(dt)
+        v = (torch.randn(1, 2, sk, D, generator=g) / math.sqrt(D)).to(dt)
+        o = st.streaming_forward(q, k, v, ni, nl)
+        out[f"c{ci}_q"], out[f"c{ci}_k"], out[f"c{ci}_v"] = bits(q), bits(k), bits(v)
+        out[f"c{ci}_meta"] = np.array([ni, nl, sq, sk, D, int(dt == torch.bfloat16)])
+        out[f"c{ci}_out"] = bits(o)
+    out["n_cases"] = np.array(len(stream_cases))
+    np.savez_compressed(os.path.join(HERE, "stream.npz"), **out)
+
+    # ---- vertical_and_slash estimation + attention ------------------------------
+    captured = {}
+
+    def _capture(q, k, v, v_idx, s_idx):
+        captured["v"] = v_idx.clone()
+        captured["s"] = s_idx.clone()
+        return vs.vertical_slash_sparse_attention(q, k, v, v_idx, s_idx)
+
+    fw._vs_sparse_attention = _capture
+    vs_cases = [
+        # (S, D, dtype, vsize, ssize, seed, sinks)
+        (200, 96, torch.bfloat16, 40, 60, 31, 4),
+        (1000, 96, torch.bfloat16, 100, 200, 32, 8),
+        (2048, 96, torch.float16, 200, 300, 33, 8),
+        (4096, 96, torch.bfloat16, 1000, 1500, 34, 32),
+    ]
+    out = {}
+    for ci, (S, D, dt, nv, ns, seed, sinks) in enumerate(vs_cases):
+        q, k, v = gen_qkv(1, 2, S, D, dt, seed, sinks=sinks)
+        o = fw._vertical_and_slash_kernel(None, q, k, v, nv, ns)
+        v_idx, s_idx = captured["v"], captured["s"]
+        # reference estimator intermediates (same expressions as :149-165)
+        last_q = min(64, S)
+        qk = torch.matmul(q[:, :, -last_q:, :], k.transpose(-2, -1)) / math.sqrt(D)
+        lq = torch.arange(last_q)
+        lq_mask = (lq[None, None, :, None] >= lq[None, None, None, :])
+        qk[:, :, :, -last_q:] = torch.where(lq_mask, qk[:, :, :, -last_q:], float("-inf"))
+        logits = qk.float()
+        p = torch.softmax(qk, dim=-1, dtype=torch.float32)
+        vert = p.sum(-2)
+        diag = fw.sum_all_diagonal_matrix(p)
+        if last_q > 1:
+            diag = diag[..., : -last_q + 1]
+        mask = vs._build_vs_mask_direct(v_idx, s_idx, S, S, q.device)
+        out[f"c{ci}_q"], out[f"c{ci}_k"], out[f"c{ci}_v"] = bits(q), bits(k), bits(v)
+        out[f"c{ci}_meta"] = np.array([S, D, int(dt == torch.bfloat16), nv, ns])
+        out[f"c{ci}_vidx"] = v_idx.numpy()
+        out[f"c{ci}_sidx"] = s_idx.numpy()
+        out[f"c{ci}_logits"] = bits(qk)
+        out[f"c{ci}_vert"] = vert.numpy()
+        out[f"c{ci}_diag"] = diag.numpy()
+        out[f"c{ci}_out"] = bits(o)
+        if S <= 2048:  # keeps the fixture small; vs_mask.npz covers the mask rules
+            out[f"c{ci}_visible"] = np.packbits((~mask).numpy(), axis=-1)
+    out["n_cases"] = np.array(len(vs_cases))
+    np.savez_compressed(os.path.join(HERE, "vertical_slash.npz"), **out)
+
+    # ---- VS direct mask on ragged / adversarial index sets ------------------------
+    g = torch.Generator().manual_seed(41)
+    out = {}
+    mcases = [(37, 5, 9), (100, 7, 20), (130, 10, 40), (257, 12, 60), (64, 3, 64), (1000, 30, 300)]
+    for ci, (S, nv, ns) in enumerate(mcases):
+        v_idx = torch.randperm(S, generator=g)[:nv].sort().values.to(torch.int32)[None, None]
+        s_idx = torch.randperm(S, generator=g)[:ns].sort(descending=True).values.to(torch.int32)[None, None]
+        mask = vs._build_vs_mask_direct(v_idx, s_idx, S, S, torch.device("cpu"))
+        out[f"c{ci}_S"] = np.array(S)
+        out[f"c{ci}_vidx"] = v_idx.numpy()
+        out[f"c{ci}_sidx"] = s_idx.numpy()
+        out[f"c{ci}_visible"] = np.packbits((~mask).numpy(), axis=-1)
+    out["n_cases"] = np.array(len(mcases))
+    np.savez_compressed(os.path.join(HERE, "vs_mask.npz"), **out)
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()
