@@ -5,11 +5,19 @@
 
 namespace mib200 {
 
+// Softmax of one 64-key block for one query row, in registers.
+// s: raw scores (overwritten).  Returns the block max of raw visible scores.
+struct RowState {
+  float m_used;  // running max (log2 domain) the current P and O are relative to
+  float l;       // running sum of P
+};
+
 template <typename DT, int D>
 __global__ void __launch_bounds__(kThreads, 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
+                    const __grid_constant__ CUtensorMap tm_v,
+                    const __grid_constant__ CUtensorMap tm_o, const AttnParams p) {
   using L = AttnSmem<D>;
   constexpr int NC = L::NC;
   constexpr bool kBF16 = DType<DT>::kBF16;
@@ -19,11 +27,13 @@ __global__ void __launch_bounds__(kThreads, 2)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = bars + 1 + kStages;
-  uint64_t* s_full = bars + 1 + 2 * kStages;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + kKStages;
+  uint64_t* v_full = k_empty + kKStages;
+  uint64_t* v_empty = v_full + kVStages;
+  uint64_t* s_full = v_empty + kVStages;
   uint64_t* p_full = s_full + 2;
-  uint64_t* pv_done = s_full + 4;
+  uint64_t* pv_done = p_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlotOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kAbortOff);
 
@@ -65,9 +75,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   // ---- one-time setup -------------------------------------------------------
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+    for (int s = 0; s < kKStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -87,33 +101,48 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 4) {
-    // ======================= TMA producer =====================================
+    // ======================= TMA producer (one thread) =========================
+    // Fixed order K0, K1, V0, K2, V1, ...: K runs one block ahead of V, and
+    // each ring slot is reused once the MMA that read it has completed.
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      uint8_t* sq = smem + L::kQOff;
       mbar_arrive_expect_tx(q_full, L::kQBytes);
       for (int c = 0; c < NC; ++c)
-        tma_load_4d(sq + c * (kBM * 64), &tm_q, q_full, c * 32, t * kBM, h, b);
-      for (int j = 0; j < n_entries; ++j) {
-        const int st = j % kStages;
-        const int use = j / kStages;
-        if (use > 0) {
-          if (!mbar_wait(&kv_empty[st], (use - 1) & 1, 101)) { *abort_flag = 1; break; }
-        }
-        if (*abort_flag) break;
+        tma_load_4d(smem + L::kQOff + c * (kBM * 64), &tm_q, q_full, c * 32, t * kBM, h, b);
+      auto load_k = [&](int j) -> bool {
+        const int st = j % kKStages, use = j / kKStages;
+        if (use > 0 && !mbar_wait(&k_empty[st], (use - 1) & 1, 101)) return false;
         int kb;
         uint64_t m0, m1;
         src.get(j, kb, m0, m1);
-        uint8_t* sk = smem + L::kKOff + st * L::kKVBytes;
-        uint8_t* sv = smem + L::kVOff + st * L::kKVBytes;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * L::kKVBytes);
-        for (int c = 0; c < NC; ++c) {
-          tma_load_4d(sk + c * (kBN * 64), &tm_k, &kv_full[st], c * 32, kb * kBN, h, b);
-          tma_load_4d(sv + c * (kBN * 64), &tm_v, &kv_full[st], c * 32, kb * kBN, h, b);
-        }
+        uint8_t* dst = smem + L::kKOff + st * L::kKVBytes;
+        mbar_arrive_expect_tx(&k_full[st], L::kKVBytes);
+        for (int c = 0; c < NC; ++c)
+          tma_load_4d(dst + c * (kBN * 64), &tm_k, &k_full[st], c * 32, kb * kBN, h, b);
+        return true;
+      };
+      auto load_v = [&](int j) -> bool {
+        const int st = j % kVStages, use = j / kVStages;
+        if (use > 0 && !mbar_wait(&v_empty[st], (use - 1) & 1, 103)) return false;
+        int kb;
+        uint64_t m0, m1;
+        src.get(j, kb, m0, m1);
+        uint8_t* dst = smem + L::kVOff + st * L::kKVBytes;
+        mbar_arrive_expect_tx(&v_full[st], L::kKVBytes);
+        for (int c = 0; c < NC; ++c)
+          tma_load_4d(dst + c * (kBN * 64), &tm_v, &v_full[st], c * 32, kb * kBN, h, b);
+        return true;
+      };
+      bool ok = true;
+      for (int j = 0; ok && j < n_entries; ++j) {
+        if (*abort_flag) break;
+        ok = load_k(j);
+        if (ok && j >= 1) ok = load_v(j - 1);
       }
+      if (ok && n_entries > 0 && !*abort_flag) ok = load_v(n_entries - 1);
+      if (!ok) *abort_flag = 1;
     }
   } else if (warp == 5) {
     // ======================= MMA issuer =======================================
@@ -123,11 +152,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t sq = smem_u32(smem + L::kQOff);
       const uint32_t sk0 = smem_u32(smem + L::kKOff);
       const uint32_t sv0 = smem_u32(smem + L::kVOff);
-      const uint32_t sp0 = smem_u32(smem + L::kPOff);
       const uint32_t tmem_o = tmem_base + 128;
 
-      auto issue_qk = [&](int j) {
-        const int st = j % kStages;
+      auto issue_qk = [&](int j) -> bool {
+        const int st = j % kKStages;
+        if (!mbar_wait(&k_full[st], (j / kKStages) & 1, 104)) return false;
+        tc_fence_after();
         const uint32_t sk = sk0 + st * L::kKVBytes;
         const uint32_t tmem_s = tmem_base + (j & 1) * kBN;
 #pragma unroll
@@ -138,36 +168,29 @@ __global__ void __launch_bounds__(kThreads, 2)
           umma_f16_ss(tmem_s, ad, bd, idesc_qk, ks > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[j & 1]);
+        umma_commit(&k_empty[st]);
+        return true;
       };
       bool ok = mbar_wait(q_full, 0, 102);
-      if (ok && n_entries > 0) {
-        ok = mbar_wait(&kv_full[0], 0, 103);
-        if (ok) {
-          tc_fence_after();
-          issue_qk(0);
-        }
-      }
+      if (ok && n_entries > 0) ok = issue_qk(0);
       for (int j = 0; ok && j < n_entries; ++j) {
-        if (*abort_flag) break;
-        if (j + 1 < n_entries) {
-          const int st = (j + 1) % kStages;
-          if (!mbar_wait(&kv_full[st], ((j + 1) / kStages) & 1, 104)) { ok = false; break; }
-          tc_fence_after();
-          issue_qk(j + 1);
-        }
+        if (*abort_flag) { ok = false; break; }
+        // S buffer (j+1)&1 last held P(j-1), consumed by PV(j-1), issued earlier by this
+        // thread: tcgen05.mma from one thread execute in issue order.
+        if (j + 1 < n_entries && !issue_qk(j + 1)) { ok = false; break; }
         if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, 105)) { ok = false; break; }
+        const int st = j % kVStages;
+        if (!mbar_wait(&v_full[st], (j / kVStages) & 1, 106)) { ok = false; break; }
         tc_fence_after();
-        const int st = j % kStages;
         const uint32_t sv = sv0 + st * L::kKVBytes;
-        const uint32_t sp = sp0 + (j & 1) * L::kPBytes;
+        const uint32_t tmem_p = tmem_base + (j & 1) * kBN;
 #pragma unroll
         for (int ks = 0; ks < kBN / 16; ++ks) {
-          const uint64_t ad = make_desc_sw64(sp + (ks >> 1) * (kBM * 64) + (ks & 1) * 32, 16, 512);
           const uint64_t bd = make_desc_sw64(sv + ks * 1024, kBN * 64, 512);
-          umma_f16_ss(tmem_o, ad, bd, idesc_pv, (j > 0 || ks > 0) ? 1u : 0u);
+          umma_f16_ts(tmem_o, tmem_p + ks * 8, bd, idesc_pv, (j > 0 || ks > 0) ? 1u : 0u);
         }
         umma_commit(&pv_done[j & 1]);
-        umma_commit(&kv_empty[st]);
+        umma_commit(&v_empty[st]);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -177,52 +200,61 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t lane_base = tmem_base + ((uint32_t)(warp * 32) << 16);
     const long long a = (long long)p.q_off + (long long)t * kBM + row;  // absolute position
     const float NEG_INF = -INFINITY;
+    const float sc = p.scale_log2;
     float m_used = NEG_INF;
     float l = 0.f;
-    uint8_t* sp_base = smem + L::kPOff;
     bool ok = true;
 
+    int kb_n = 0;
+    uint64_t m0_n = 0, m1_n = 0;
+    if (n_entries > 0) src.get(0, kb_n, m0_n, m1_n);
     for (int j = 0; j < n_entries; ++j) {
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, 106)) { ok = false; break; }
-      tc_fence_after();
-      float s[kBN];
-      tmem_ld32(lane_base + (j & 1) * kBN, *reinterpret_cast<float(*)[32]>(&s[0]));
-      tmem_ld32(lane_base + (j & 1) * kBN + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
-      tmem_wait_ld();
+      const int kb = kb_n;
+      const uint64_t mask = (row < 64) ? m0_n : m1_n;
+      if (j + 1 < n_entries) src.get(j + 1, kb_n, m0_n, m1_n);  // prefetch next entry
 
-      int kb;
-      uint64_t m0, m1;
-      src.get(j, kb, m0, m1);
-      const uint64_t mask = (row < 64) ? m0 : m1;
+      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, 107)) { ok = false; break; }
+      tc_fence_after();
+
       const long long key0 = (long long)kb * kBN;
-      // Visible keys of this row inside the block form: mask AND key <= a AND key < Sk AND
-      // (key < n_init OR key > a - n_local).  Fast path when all 64 are visible.
-      const bool full = (mask == ~0ull) && (key0 + kBN - 1 <= a) && (key0 + kBN - 1 < p.Sk) &&
-                        (key0 > a - p.n_local || key0 + kBN - 1 < p.n_init);
+      // Visible keys of this row inside the block:
+      //   mask AND key <= a AND key < Sk AND (key < n_init OR key > a - n_local).
+      const uint64_t vis = mask & bits_below(a - key0 + 1) & bits_below((long long)p.Sk - key0) &
+                           (bits_below(p.n_init - key0) | ~bits_below(a - p.n_local - key0 + 1));
+      const bool all_full = __all_sync(0xffffffffu, vis == ~0ull);
+      const bool all_empty = __all_sync(0xffffffffu, vis == 0ull);
+      const uint32_t tmem_s = lane_base + (j & 1) * kBN;
+
+      float s[kBN];
       float tmax = NEG_INF;
-      if (full) {
+      if (!all_empty) {
+        tmem_ld32(tmem_s, *reinterpret_cast<float(*)[32]>(&s[0]));
+        tmem_ld32(tmem_s + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
+        tmem_wait_ld();
+        if (!all_full) {
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) {
-          s[c] *= p.scale_log2;
-          tmax = fmaxf(tmax, s[c]);
+          for (int c = 0; c < kBN; ++c) s[c] = ((vis >> c) & 1ull) ? s[c] : NEG_INF;
         }
-      } else {
+        float mx0 = fmax3(s[0], s[1], s[2]);
+        float mx1 = fmax3(s[3], s[4], s[5]);
+        float mx2 = fmax3(s[6], s[7], s[8]);
+        float mx3 = fmax3(s[9], s[10], s[11]);
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) {
-          const long long key = key0 + c;
-          const bool vis = ((mask >> c) & 1ull) && key <= a && key < p.Sk &&
-                           (key < p.n_init || key > a - p.n_local);
-          s[c] = vis ? s[c] * p.scale_log2 : NEG_INF;
-          tmax = fmaxf(tmax, s[c]);
+        for (int c = 12; c < 60; c += 8) {
+          mx0 = fmax3(mx0, s[c], s[c + 1]);
+          mx1 = fmax3(mx1, s[c + 2], s[c + 3]);
+          mx2 = fmax3(mx2, s[c + 4], s[c + 5]);
+          mx3 = fmax3(mx3, s[c + 6], s[c + 7]);
         }
+        tmax = fmaxf(fmax3(mx0, mx1, fmax3(s[60], s[61], s[62])), fmax3(mx2, mx3, s[63]));
       }
-      const float m_new = fmaxf(m_used, tmax);
+      const float m_new = fmaxf(m_used, tmax * sc);
       const bool need = m_new > m_used + 8.0f;
       if (j == 0) {
         m_used = m_new;
       } else if (__any_sync(0xffffffffu, need)) {
         // O must hold PV(j-1) before it is rescaled.
-        if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, 107)) { ok = false; break; }
+        if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, 108)) { ok = false; break; }
         tc_fence_after();
         const float f = need ? ((m_used == NEG_INF) ? 0.f : fast_exp2(m_used - m_new)) : 1.f;
 #pragma unroll
@@ -240,48 +272,52 @@ __global__ void __launch_bounds__(kThreads, 2)
           m_used = m_new;
         }
       }
-      // P = exp2(s - m_used); rows with nothing visible yet keep P = 0.
-      float lsum = 0.f;
+      // P = 2^(s*scale_log2 - m_used); rows with nothing visible yet keep P = 0.
       uint32_t pk[kBN / 2];
-      if (m_used == NEG_INF) {
+      float ls0 = 0.f, ls1 = 0.f;
+      if (all_empty || m_used == NEG_INF) {
 #pragma unroll
         for (int c = 0; c < kBN / 2; ++c) pk[c] = 0u;
       } else {
+        const uint64_t sc2 = pk2(sc, sc);
+        const uint64_t nm2 = pk2(-m_used, -m_used);
+        uint64_t acc0 = pk2(0.f, 0.f), acc1 = pk2(0.f, 0.f);
 #pragma unroll
         for (int c = 0; c < kBN / 2; ++c) {
-          const float p0 = fast_exp2(s[2 * c] - m_used);
-          const float p1 = fast_exp2(s[2 * c + 1] - m_used);
-          lsum += p0 + p1;
+          const uint64_t x2 = ffma2(pk2(s[2 * c], s[2 * c + 1]), sc2, nm2);
+          float p0, p1;
+          if (all_full && (c & 3) == 3) {  // one pair in four on the FMA pipe
+            float x0, x1;
+            upk2(x2, x0, x1);
+            poly_exp2x2(pk2(fmaxf(x0, -127.f), fmaxf(x1, -127.f)), p0, p1);
+          } else {
+            float x0, x1;
+            upk2(x2, x0, x1);
+            p0 = fast_exp2(x0);
+            p1 = fast_exp2(x1);
+          }
+          if (c & 1)
+            acc1 = fadd2(acc1, pk2(p0, p1));
+          else
+            acc0 = fadd2(acc0, pk2(p0, p1));
           pk[c] = DType<DT>::pack2(p0, p1);
         }
+        acc0 = fadd2(acc0, acc1);
+        upk2(acc0, ls0, ls1);
       }
-      l += lsum;
-      // P buffer (j & 1) was last read by PV(j-2).
-      if (j >= 2) {
-        if (!mbar_wait(&pv_done[j & 1], ((j - 2) >> 1) & 1, 108)) { ok = false; break; }
-      }
-      uint8_t* sp = sp_base + (j & 1) * L::kPBytes;
-      const uint32_t sw = (row >> 1) & 3;
-#pragma unroll
-      for (int pc = 0; pc < 2; ++pc) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          uint4 val = make_uint4(pk[pc * 16 + u * 4 + 0], pk[pc * 16 + u * 4 + 1],
-                                 pk[pc * 16 + u * 4 + 2], pk[pc * 16 + u * 4 + 3]);
-          *reinterpret_cast<uint4*>(sp + pc * (kBM * 64) + row * 64 + ((u ^ sw) << 4)) = val;
-        }
-      }
-      fence_proxy_async_smem();
+      l += ls0 + ls1;
+      // P(j) overwrites the first 32 columns of S buffer (j & 1).
+      tmem_st32u(tmem_s, pk);
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[j & 1]);
     }
 
-    // ---- epilogue: O / l -> out ---------------------------------------------
+    // ---- epilogue: O / l -> shared (Q tile area, swizzled) -> TMA store -----
     if (!ok) *abort_flag = 1;
-    const long long qrow = (long long)t * kBM + row;
-    float o[D];
     bool have_o = false;
-    if (ok && n_entries > 0 && !*abort_flag) {
+    float o[D];
+    if (ok && n_entries > 0) {
       const int jl = n_entries - 1;
       if (mbar_wait(&pv_done[jl & 1], (jl >> 1) & 1, 109)) {
         tc_fence_after();
@@ -291,22 +327,35 @@ __global__ void __launch_bounds__(kThreads, 2)
         tmem_wait_ld();
         have_o = true;
       } else {
-        *abort_flag = 1;
+        ok = false;
+      }
+    } else if (ok) {
+      ok = mbar_wait(q_full, 0, 110);  // the Q tile area must be idle before reuse
+    }
+    if (!ok) *abort_flag = 1;
+    const float inv = (have_o && l > 0.f) ? 1.f / l : 0.f;
+    const uint32_t sw = (row >> 1) & 3;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int e = c * 32 + u * 8;
+        uint4 val;
+        val.x = DType<DT>::pack2(have_o ? o[e + 0] * inv : 0.f, have_o ? o[e + 1] * inv : 0.f);
+        val.y = DType<DT>::pack2(have_o ? o[e + 2] * inv : 0.f, have_o ? o[e + 3] * inv : 0.f);
+        val.z = DType<DT>::pack2(have_o ? o[e + 4] * inv : 0.f, have_o ? o[e + 5] * inv : 0.f);
+        val.w = DType<DT>::pack2(have_o ? o[e + 6] * inv : 0.f, have_o ? o[e + 7] * inv : 0.f);
+        *reinterpret_cast<uint4*>(smem + L::kQOff + c * (kBM * 64) + row * 64 + ((u ^ sw) << 4)) =
+            val;
       }
     }
-    if (qrow < p.Sq) {
-      const float inv = (have_o && l > 0.f) ? 1.f / l : 0.f;
-      DT* dst = reinterpret_cast<DT*>(p.out) + (long long)b * p.os_b + (long long)h * p.os_h +
-                qrow * p.os_s;
-#pragma unroll
-      for (int c = 0; c < D / 8; ++c) {
-        uint4 val;
-        val.x = DType<DT>::pack2(have_o ? o[8 * c + 0] * inv : 0.f, have_o ? o[8 * c + 1] * inv : 0.f);
-        val.y = DType<DT>::pack2(have_o ? o[8 * c + 2] * inv : 0.f, have_o ? o[8 * c + 3] * inv : 0.f);
-        val.z = DType<DT>::pack2(have_o ? o[8 * c + 4] * inv : 0.f, have_o ? o[8 * c + 5] * inv : 0.f);
-        val.w = DType<DT>::pack2(have_o ? o[8 * c + 6] * inv : 0.f, have_o ? o[8 * c + 7] * inv : 0.f);
-        *reinterpret_cast<uint4*>(dst + 8 * c) = val;
-      }
+    fence_proxy_async_smem();
+    named_barrier(1, kBM);
+    if (row == 0 && !*abort_flag) {
+      for (int c = 0; c < NC; ++c)
+        tma_store_4d(&tm_o, smem + L::kQOff + c * (kBM * 64), c * 32, t * kBM, h, b);
+      bulk_commit();
+      bulk_wait_read0();
     }
   }
 
@@ -323,19 +372,20 @@ __global__ void __launch_bounds__(kThreads, 2)
 // ---------------------------------------------------------------------------
 template <typename DT, int D>
 static int launch_attn_t(const mi_tensor4& q, const mi_tensor4& k, const mi_tensor4& v,
-                         AttnParams prm, cudaStream_t stream) {
+                         const mi_tensor4& out, AttnParams prm, cudaStream_t stream) {
   using L = AttnSmem<D>;
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;
   int rc;
   if ((rc = make_bnsd_map(&tq, q, prm.B, prm.H, prm.Sq, D, 32, kBM)) != MI_OK) return rc;
   if ((rc = make_bnsd_map(&tk, k, prm.B, prm.H, prm.Sk, D, 32, kBN)) != MI_OK) return rc;
   if ((rc = make_bnsd_map(&tv, v, prm.B, prm.H, prm.Sk, D, 32, kBN)) != MI_OK) return rc;
+  if ((rc = make_bnsd_map(&to, out, prm.B, prm.H, prm.Sq, D, 32, kBM)) != MI_OK) return rc;
   auto kern = attn_fwd_kernel<DT, D>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc) !=
       cudaSuccess)
     return MI_ERR_LAUNCH;
   dim3 grid(prm.T, prm.H, prm.B);
-  kern<<<grid, kThreads, L::kAlloc, stream>>>(tq, tk, tv, prm);
+  kern<<<grid, kThreads, L::kAlloc, stream>>>(tq, tk, tv, to, prm);
   return cudaGetLastError() == cudaSuccess ? MI_OK : MI_ERR_LAUNCH;
 }
 
@@ -347,14 +397,11 @@ int launch_attention(const mi_tensor4& q, const mi_tensor4& k, const mi_tensor4&
   prm.os_h = out.stride_h;
   prm.os_s = out.stride_s;
   if (prm.T == 0 || prm.H == 0 || prm.B == 0) return MI_OK;
-  if (out.stride_d != 1 || (reinterpret_cast<uintptr_t>(out.ptr) & 15) || (out.stride_s * 2) % 16 ||
-      (out.stride_h * 2) % 16 || (out.stride_b * 2) % 16)
-    return MI_ERR_ALIGN;
   const bool bf = dtype == MI_BF16;
 #define MI_ATTN_CASE(DD)                                                            \
   if (D == DD)                                                                     \
-    return bf ? launch_attn_t<__nv_bfloat16, DD>(q, k, v, prm, stream)             \
-              : launch_attn_t<__half, DD>(q, k, v, prm, stream);
+    return bf ? launch_attn_t<__nv_bfloat16, DD>(q, k, v, out, prm, stream)        \
+              : launch_attn_t<__half, DD>(q, k, v, out, prm, stream);
   MI_ATTN_CASE(64)
   MI_ATTN_CASE(96)
   MI_ATTN_CASE(128)

@@ -15,13 +15,18 @@
 //
 // Warp roles (192 threads):
 //   warps 0-3  softmax: thread r owns query row r of the tile; reads S from
-//              TMEM, applies masks, online softmax in registers (exp2),
-//              writes P (bf16/fp16) to shared memory, rescales O in TMEM when
-//              the running max grows by more than 2^8, final normalisation.
-//   warp 4     TMA producer: Q once, then K and V blocks into a 2-stage ring.
+//              TMEM, applies masks, online softmax in registers (exp2 on the
+//              MUFU unit for 3/4 of the elements, a degree-3 polynomial on the
+//              FMA pipe for the rest), writes P (bf16/fp16) back into the same
+//              TMEM columns, rescales O in TMEM when the running max grows by
+//              more than 2^8, final normalisation and TMA store of the tile.
+//   warp 4     TMA producer: Q once, then K blocks into a 4-deep ring and V
+//              blocks into a 3-deep ring (K runs ahead because S = QK^T is
+//              issued one block ahead of O += PV).
 //   warp 5     TMEM allocator + single-thread tcgen05.mma issuer:
-//              S = Q K^T (M=128, N=64, K=D) into a double-buffered TMEM tile,
-//              O += P V (M=128, N=D, K=64) into TMEM.
+//              S = Q K^T (M=128, N=64, K=D, both operands in shared memory)
+//              into a double-buffered TMEM tile; O += P V (M=128, N=D, K=64)
+//              with P read from TMEM and V from shared memory.
 #pragma once
 #include "common.cuh"
 
@@ -61,27 +66,29 @@ struct AttnParams {
 
 constexpr int kBM = 128;       // query rows per CTA
 constexpr int kBN = 64;        // keys per KV block
-constexpr int kStages = 2;     // KV ring depth
+constexpr int kKStages = 4;    // K ring depth (K runs ahead of V)
+constexpr int kVStages = 3;    // V ring depth
 constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 256;  // S0 [0,64), S1 [64,128), O [128,128+D)
+constexpr uint32_t kTmemCols = 256;  // S0 [0,64), S1 [64,128), O [128,128+D); P(j) aliases S(j&1)
 
 template <int D>
 struct AttnSmem {
   static constexpr int NC = D / 32;                 // 64-byte chunks per row
-  static constexpr int kQBytes = NC * kBM * 64;     // Q tile
+  static constexpr int kQBytes = NC * kBM * 64;     // Q tile (reused for the output tile)
   static constexpr int kKVBytes = NC * kBN * 64;    // one K (or V) block
-  static constexpr int kPBytes = 2 * kBM * 64;      // one P buffer (64 keys)
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kQOff + kQBytes;
-  static constexpr int kVOff = kKOff + kStages * kKVBytes;
-  static constexpr int kPOff = kVOff + kStages * kKVBytes;
-  static constexpr int kBarOff = kPOff + 2 * kPBytes;
-  // barriers: q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], pv_done[2]
-  static constexpr int kNumBars = 1 + 2 * kStages + 6;
+  static constexpr int kVOff = kKOff + kKStages * kKVBytes;
+  static constexpr int kBarOff = kVOff + kVStages * kKVBytes;
+  // barriers: q_full, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
+  //           s_full[2], p_full[2], pv_done[2]
+  static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 6;
   static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
   static constexpr int kAbortOff = kTmemSlotOff + 4;
   static constexpr int kBytes = kAbortOff + 4;
-  static constexpr int kAlloc = kBytes + 1024;      // room to align the base to 1 KiB
+  // +1 KiB to align the base; never less than ~80 KiB so at most two CTAs
+  // share an SM (two CTAs use all 512 TMEM columns).
+  static constexpr int kAlloc = (kBytes + 1024) > 80 * 1024 ? (kBytes + 1024) : 80 * 1024;
 };
 
 // Entry j of the current tile (identical result in every warp that asks).

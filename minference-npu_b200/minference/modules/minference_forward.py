@@ -1,0 +1,260 @@
+"""Patched attention forward: per-head pattern dispatch onto the sm_100a ops.
+
+Mirrors the reference dispatcher (MInference-NPU
+minference/modules/minference_forward.py:175-502):
+
+* ``init_minference_parameters`` reads ``starting_layer``, ``config_path`` and
+  ``minference_attn_type`` from the model config and this layer's entry of
+  the pattern JSON (:175-213);
+* the forward does the fused QKV projection, RoPE, cache update and
+  ``repeat_kv`` (:300-372), then either runs every head dense
+  (``attn_type == "dense"`` or ``layer_idx < starting_layer``, :388-396) or
+  groups heads by ``(type, sizes)`` with the reference's default
+  ``("vertical_and_slash", 1000, 6096)`` for unlisted heads (:398-419) and
+  launches one op per group (:423-487);
+* ``o_proj`` on the re-assembled heads (:492-494).
+
+Differences in how the work is laid out (results are the same): a group
+whose heads form a contiguous range is passed as a strided view and written
+in place into the layer output (no ``index_select`` / ``index_copy_``);
+other groups gather their heads.  The layer output is allocated in the
+``[B, S, H, D]`` layout ``o_proj`` consumes, and the ops write into its
+``[B, H, S, D]`` view.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+from importlib import import_module
+
+import torch
+
+from .. import ops as _ops
+
+__all__ = [
+    "init_minference_parameters",
+    "minference_forward",
+    "gather_last_q_sparse_topk",
+    "load_pattern_config",
+    "group_heads",
+    "DEFAULT_PATTERN",
+    "PATTERN_TYPES",
+]
+
+DEFAULT_PATTERN = ("vertical_and_slash", 1000, 6096, 1)
+PATTERN_TYPES = ("vertical_and_slash", "stream_llm", "block_sparse", "dense")
+
+# The op table used by the dispatcher.  Tests may swap in a recording stub.
+OPS = _ops
+
+
+# ----------------------------------------------------------------------------
+# Pattern config
+# ----------------------------------------------------------------------------
+
+
+def load_pattern_config(src, num_layers: int | None = None, num_heads: int | None = None):
+    """Load and validate a per-head pattern config.
+
+    ``src`` is a path to the JSON file or an already-parsed list.  Returns a
+    list with one ``{head: (type, v, s, score)}`` dict per layer.  Raises
+    ValueError on unknown pattern types, malformed entries, head ids out of
+    range or non-positive sizes."""
+    if isinstance(src, (str, os.PathLike)):
+        with open(src) as f:
+            data = json.load(f)
+    else:
+        data = src
+    if not isinstance(data, list):
+        raise ValueError("pattern config must be a list with one dict per layer")
+    if num_layers is not None and len(data) > num_layers:
+        raise ValueError(f"pattern config has {len(data)} layers, model has {num_layers}")
+    out = []
+    for li, layer in enumerate(data):
+        if not isinstance(layer, dict):
+            raise ValueError(f"layer {li}: expected a dict of head -> pattern")
+        parsed = {}
+        for key, val in layer.items():
+            try:
+                head = int(key)
+            except (TypeError, ValueError):
+                raise ValueError(f"layer {li}: head id {key!r} is not an integer") from None
+            if head < 0 or (num_heads is not None and head >= num_heads):
+                raise ValueError(f"layer {li}: head id {head} out of range")
+            if not isinstance(val, (list, tuple)) or len(val) < 3:
+                raise ValueError(f"layer {li} head {head}: expected [type, v, s, score]")
+            ty = val[0]
+            if ty not in PATTERN_TYPES:
+                raise ValueError(
+                    f"layer {li} head {head}: unsupported pattern {ty!r}; "
+                    f"supported: {', '.join(PATTERN_TYPES)}"
+                )
+            v, s = int(val[1]), int(val[2])
+            score = val[3] if len(val) > 3 else 1
+            if ty == "vertical_and_slash" and (v <= 0 or s <= 0):
+                raise ValueError(f"layer {li} head {head}: vertical/slash sizes must be > 0")
+            if ty == "block_sparse" and v <= 0:
+                raise ValueError(f"layer {li} head {head}: block_sparse top-k must be > 0")
+            if ty == "stream_llm" and (v < 0 or s <= 0):
+                raise ValueError(f"layer {li} head {head}: stream_llm needs n_init >= 0, n_local > 0")
+            parsed[head] = (ty, v, s, score)
+        out.append(parsed)
+    return out
+
+
+def group_heads(best_pattern: dict, num_heads: int):
+    """[(key, heads)] in the reference's launch order: VS groups, dense,
+    stream groups, block_sparse groups.  key = (type, params...)."""
+    vs, stream, block, dense = {}, {}, {}, []
+    for h in range(num_heads):
+        ty, v, s, _ = best_pattern.get(h, DEFAULT_PATTERN)
+        if ty == "vertical_and_slash":
+            vs.setdefault((int(v), int(s)), []).append(h)
+        elif ty == "stream_llm":
+            stream.setdefault((int(v), int(s)), []).append(h)
+        elif ty == "block_sparse":
+            block.setdefault(int(v), []).append(h)
+        elif ty == "dense":
+            dense.append(h)
+        else:
+            raise ValueError(f"unknown pattern type {ty!r}")
+    groups = [(("vertical_and_slash", v, s), hs) for (v, s), hs in vs.items()]
+    if dense:
+        groups.append((("dense",), dense))
+    groups += [(("stream_llm", n, l), hs) for (n, l), hs in stream.items()]
+    groups += [(("block_sparse", k), hs) for k, hs in block.items()]
+    return groups
+
+
+# ----------------------------------------------------------------------------
+# Per-layer initialisation
+# ----------------------------------------------------------------------------
+
+
+def init_minference_parameters(self) -> None:
+    if getattr(self, "_minference_initialized", False):
+        return
+    cfg = self.config
+    self.starting_layer = getattr(cfg, "starting_layer", 0)
+    if self.starting_layer is None:
+        self.starting_layer = 0
+    self.is_search = getattr(cfg, "is_search", False)
+    self.config_path = getattr(cfg, "config_path", "") or ""
+    self._minference_attn_type = getattr(cfg, "minference_attn_type", "minference")
+    patterns = getattr(cfg, "minference_best_pattern", None)
+    if patterns is None and self.config_path and os.path.exists(self.config_path):
+        patterns = load_pattern_config(self.config_path, num_heads=cfg.num_attention_heads)
+    elif patterns is not None:
+        patterns = load_pattern_config(patterns, num_heads=cfg.num_attention_heads)
+    if patterns is not None and self.layer_idx < len(patterns):
+        self.best_pattern = patterns[self.layer_idx]
+    else:
+        self.best_pattern = {}
+    module = import_module(self.__class__.__module__)
+    self._apply_rotary = getattr(module, "apply_rotary_pos_emb")
+    self._minference_initialized = True
+
+
+# ----------------------------------------------------------------------------
+# Single-head compatibility dispatcher (reference :216-250)
+# ----------------------------------------------------------------------------
+
+
+def _run_pattern(key, q, k, v, out=None):
+    ty = key[0]
+    if ty == "vertical_and_slash":
+        return OPS.vertical_and_slash(q, k, v, key[1], key[2], out=out)
+    if ty == "stream_llm":
+        return OPS.streaming_forward(q, k, v, key[1], key[2], out=out)
+    if ty == "block_sparse":
+        return OPS.block_sparse_attention(q, k, v, key[1], out=out)
+    if ty == "dense":
+        return OPS.dense_attention(q, k, v, causal=True, out=out)
+    raise NotImplementedError(f"Unsupported pattern {ty!r}")
+
+
+def gather_last_q_sparse_topk(self, q, k, v, head_id: int):
+    """Run one head's configured pattern on BNSD q/k/v (kept for old call sites)."""
+    if q.shape[2] == 1:
+        return OPS.dense_attention(q, k, v, causal=True)
+    ty, vs, ss, _ = self.best_pattern.get(head_id, DEFAULT_PATTERN)
+    if ty == "block_sparse":
+        key = ("block_sparse", int(vs))
+    elif ty == "dense":
+        key = ("dense",)
+    else:
+        key = (ty, int(vs), int(ss))
+    return _run_pattern(key, q, k, v)
+
+
+# ----------------------------------------------------------------------------
+# Layer attention
+# ----------------------------------------------------------------------------
+
+
+def _contiguous_range(heads):
+    return heads == list(range(heads[0], heads[0] + len(heads)))
+
+
+def attention_heads(self, q, k, v):
+    """q/k/v BNSD (after RoPE and repeat_kv) -> output [B, S, H, D]."""
+    B, H, S, D = q.shape
+    out_bshd = torch.empty((B, S, H, D), dtype=q.dtype, device=q.device)
+    out = out_bshd.transpose(1, 2)
+    if S == 1 or self._minference_attn_type == "dense" or self.layer_idx < self.starting_layer \
+            or self.is_search:
+        OPS.dense_attention(q, k, v, causal=True, out=out)
+        return out_bshd
+    for key, heads in group_heads(self.best_pattern, H):
+        if _contiguous_range(heads):
+            sl = slice(heads[0], heads[-1] + 1)
+            _run_pattern(key, q[:, sl], k[:, sl], v[:, sl], out=out[:, sl])
+        else:
+            idx = torch.tensor(heads, device=q.device, dtype=torch.long)
+            res = _run_pattern(key, q.index_select(1, idx), k.index_select(1, idx),
+                               v.index_select(1, idx))
+            out.index_copy_(1, idx, res)
+    return out_bshd
+
+
+def minference_forward():
+    """Forward bound onto HF Phi-3 / Llama-family attention modules
+    (transformers 5.x: returns ``(attn_output, None)``)."""
+
+    def forward(self, hidden_states, position_embeddings=None, attention_mask=None,
+                past_key_values=None, **kwargs):
+        self.init_minference_parameters()
+        bsz, q_len, _ = hidden_states.shape
+        cfg = self.config
+        n_heads = cfg.num_attention_heads
+        n_kv = cfg.num_key_value_heads
+        hd = self.head_dim
+        if "qkv_proj" in self._modules:
+            qkv = self.qkv_proj(hidden_states)
+            qp = n_heads * hd
+            kvp = n_kv * hd
+            query_states, key_states, value_states = torch.split(qkv, [qp, kvp, kvp], -1)
+        else:
+            query_states = self.q_proj(hidden_states)
+            key_states = self.k_proj(hidden_states)
+            value_states = self.v_proj(hidden_states)
+        query_states = query_states.view(bsz, q_len, n_heads, hd).transpose(1, 2)
+        key_states = key_states.view(bsz, q_len, n_kv, hd).transpose(1, 2)
+        value_states = value_states.view(bsz, q_len, n_kv, hd).transpose(1, 2)
+        if position_embeddings is None:
+            position_embeddings = kwargs.get("position_embeddings")
+        cos, sin = position_embeddings
+        query_states, key_states = self._apply_rotary(query_states, key_states, cos, sin)
+        if past_key_values is not None:
+            key_states, value_states = past_key_values.update(key_states, value_states,
+                                                              self.layer_idx)
+        n_rep = n_heads // n_kv
+        if n_rep > 1:
+            key_states = key_states.repeat_interleave(n_rep, dim=1)
+            value_states = value_states.repeat_interleave(n_rep, dim=1)
+        out_bshd = attention_heads(self, query_states, key_states, value_states)
+        attn_output = self.o_proj(out_bshd.reshape(bsz, q_len, n_heads * hd))
+        return attn_output, None
+
+    return forward
