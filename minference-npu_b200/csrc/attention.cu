@@ -5,6 +5,28 @@
 
 namespace mib200 {
 
+// Tuning knobs (compile-time):
+//   MI_POLY_MASK   pair index c uses the FMA-pipe exp2 when (c & MI_POLY_MASK) == MI_POLY_MASK
+//                  (3: one pair in four, 1: one in two)
+//   MI_PACK_INT    1: round P to 16 bits with integer ops + byte permute (ALU pipe)
+//                  instead of the cvt.rn.bf16x2 conversion
+#ifndef MI_POLY_MASK
+#define MI_POLY_MASK 3
+#endif
+#ifndef MI_PACK_INT
+#define MI_PACK_INT 0
+#endif
+
+// bf16x2 from two non-negative floats: round half up on the dropped 16 bits,
+// then keep the high halves (one PRMT).  Used for P (values in [0, 256]).
+__device__ __forceinline__ uint32_t pack_bf16_int(float a, float b) {
+  const uint32_t ua = __float_as_uint(a) + 0x8000u;
+  const uint32_t ub = __float_as_uint(b) + 0x8000u;
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(r) : "r"(ua), "r"(ub));
+  return r;
+}
+
 // Softmax of one 64-key block for one query row, in registers.
 // s: raw scores (overwritten).  Returns the block max of raw visible scores.
 struct RowState {
@@ -286,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int c = 0; c < kBN / 2; ++c) {
           const uint64_t x2 = ffma2(pk2(s[2 * c], s[2 * c + 1]), sc2, nm2);
           float p0, p1;
-          if (all_full && (c & 3) == 3) {  // one pair in four on the FMA pipe
+          if (all_full && (c & MI_POLY_MASK) == MI_POLY_MASK) {  // share of pairs on the FMA pipe
             float x0, x1;
             upk2(x2, x0, x1);
             poly_exp2x2(pk2(fmaxf(x0, -127.f), fmaxf(x1, -127.f)), p0, p1);
@@ -300,7 +322,15 @@ __global__ void __launch_bounds__(kThreads, 2)
             acc1 = fadd2(acc1, pk2(p0, p1));
           else
             acc0 = fadd2(acc0, pk2(p0, p1));
+#if MI_PACK_INT
+          if constexpr (kBF16) {
+            pk[c] = pack_bf16_int(p0, p1);
+          } else {
+            pk[c] = DType<DT>::pack2(p0, p1);
+          }
+#else
           pk[c] = DType<DT>::pack2(p0, p1);
+#endif
         }
         acc0 = fadd2(acc0, acc1);
         upk2(acc0, ls0, ls1);

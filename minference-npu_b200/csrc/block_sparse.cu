@@ -52,41 +52,112 @@ __global__ void __launch_bounds__(256) pool_kernel(mi_tensor4 q, mi_tensor4 k, i
 }
 
 // ---------------------------------------------------------------------------
-// K2: scores + top-k for one (b, h, query block).  score(kb) = fmaf chain over
-// d = 0..D-1 of q_pool[d] * k_pool[kb][d], times score_scale.  Key blocks
-// kb > bq score -inf.  With force_sink_diag, blocks 0 and bq rank above all.
+// K1 (vectorised): same result as pool_kernel, 16-byte loads.  One thread
+// owns 8 consecutive dims of one 64-row block and adds the 64 rows in row
+// order.  Needs D % 8 == 0 and 16-byte aligned rows.  Grid
+// (ceil(max(nbq,nbk)/8), H, 2B): z = 2b + (0: q, 1: k).  Block 8 * D/8 threads.
+// ---------------------------------------------------------------------------
+template <typename DT>
+__global__ void __launch_bounds__(128) pool_kernel_v(mi_tensor4 q, mi_tensor4 k, int H, int Sq,
+                                                     int Sk, int D, int nbq, int nbk,
+                                                     float* q_pool, float* k_poolT) {
+  const int chunks = D / 8;
+  const int u = threadIdx.x / chunks, c = threadIdx.x % chunks;
+  const int blk = blockIdx.x * 8 + u;
+  const int h = blockIdx.y, b = blockIdx.z >> 1;
+  const bool is_k = blockIdx.z & 1;
+  const int bh = b * H + h;
+  const int S = is_k ? Sk : Sq;
+  const int nb = is_k ? nbk : nbq;
+  if (u >= 8 || blk >= nb) return;
+  const mi_tensor4& t = is_k ? k : q;
+  const uint16_t* base = reinterpret_cast<const uint16_t*>(t.ptr) + (long long)b * t.stride_b +
+                         (long long)h * t.stride_h + (long long)blk * 64 * t.stride_s + c * 8;
+  const int rn = min(64, S - blk * 64);
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll 1
+  for (int r0 = 0; r0 < 64; r0 += 16) {
+    uint4 raw[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r)
+      raw[r] = (r0 + r < rn) ? *reinterpret_cast<const uint4*>(base + (long long)(r0 + r) * t.stride_s)
+                             : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      const uint16_t* hv = reinterpret_cast<const uint16_t*>(&raw[r]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = __fadd_rn(acc[e], DType<DT>::to_f(hv[e]));
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float pooled = DType<DT>::round(__fdiv_rn(acc[e], 64.f));
+    const int d = c * 8 + e;
+    if (is_k)
+      k_poolT[((long long)bh * D + d) * nbk + blk] = pooled;
+    else
+      q_pool[((long long)bh * nbq + blk) * D + d] = pooled;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// K2: scores + top-k for kRows consecutive query blocks of one (b, h).
+// score(bq, kb) = fmaf chain over d = 0..D-1 of q_pool[bq][d] * k_pool[kb][d],
+// times score_scale; key blocks kb > bq score -inf; with force_sink_diag
+// blocks 0 and bq rank above everything.  Every pooled-K value read from L2
+// serves kRows query blocks.  Then warp w selects the top-k of row w.
+// Dynamic shared memory: kRows * nbk keys + kRows * D floats.
 // ---------------------------------------------------------------------------
 constexpr int kSelThreads = 256;
-constexpr int kMaxBlocks = 8192;  // S up to 512K tokens
+constexpr int kSelRows = 8;        // query blocks per CTA (one selecting warp each)
+constexpr int kMaxBlocks = 8192;   // S up to 512K tokens
 
 __global__ void __launch_bounds__(kSelThreads) block_select_kernel(
     const float* q_pool, const float* k_poolT, int H, int D, int nbq, int nbk, int topk,
     int force_sink_diag, float score_scale, int64_t* out_idx) {
-  __shared__ uint32_t keys[kMaxBlocks];
-  __shared__ float qv[256];
-  __shared__ TopkSmem<kSelThreads> tsm;
-  const int bq = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  extern __shared__ uint32_t sel_smem[];
+  uint32_t* keys = sel_smem;                                          // [kSelRows][nbk]
+  float* qv = reinterpret_cast<float*>(sel_smem + kSelRows * nbk);    // [kSelRows][D]
+  __shared__ int hist[kSelRows][256];
+  const int bq0 = blockIdx.x * kSelRows, h = blockIdx.y, b = blockIdx.z;
   const int bh = b * H + h;
-  for (int d = threadIdx.x; d < D; d += kSelThreads) qv[d] = q_pool[((long long)bh * nbq + bq) * D + d];
+  const int rows = min(kSelRows, nbq - bq0);
+  for (int e = threadIdx.x; e < kSelRows * D; e += kSelThreads) {
+    const int r = e / D, d = e % D;
+    qv[e] = (r < rows) ? q_pool[((long long)bh * nbq + bq0 + r) * D + d] : 0.f;
+  }
   __syncthreads();
   const float* kp = k_poolT + (long long)bh * D * nbk;
   const uint32_t kNegInf = float_to_ordered(-INFINITY);
+  const int last_bq = bq0 + rows - 1;
   for (int kb = threadIdx.x; kb < nbk; kb += kSelThreads) {
-    uint32_t key;
-    if (kb > bq) {
-      key = kNegInf;
-    } else {
-      float acc = 0.f;
-      for (int d = 0; d < D; ++d) acc = __fmaf_rn(qv[d], kp[(long long)d * nbk + kb], acc);
-      key = float_to_ordered(__fmul_rn(acc, score_scale));
+    float acc[kSelRows];
+#pragma unroll
+    for (int r = 0; r < kSelRows; ++r) acc[r] = 0.f;
+    if (kb <= last_bq) {
+      for (int d = 0; d < D; ++d) {
+        const float kv = kp[(long long)d * nbk + kb];
+#pragma unroll
+        for (int r = 0; r < kSelRows; ++r) acc[r] = __fmaf_rn(qv[r * D + d], kv, acc[r]);
+      }
     }
-    if (force_sink_diag && (kb == 0 || kb == bq)) key = 0xFFFFFFFFu;
-    keys[kb] = key;
+#pragma unroll
+    for (int r = 0; r < kSelRows; ++r) {
+      const int bq = bq0 + r;
+      uint32_t key = (kb > bq) ? kNegInf : float_to_ordered(__fmul_rn(acc[r], score_scale));
+      if (force_sink_diag && (kb == 0 || kb == bq)) key = 0xFFFFFFFFu;
+      keys[r * nbk + kb] = key;
+    }
   }
   __syncthreads();
-  const int kk = min(topk, nbk);
-  int64_t* dst = out_idx + ((long long)bh * nbq + bq) * kk;
-  block_topk<kSelThreads>(keys, nbk, kk, tsm, [&](int pos, int idx) { dst[pos] = idx; });
+  const int w = threadIdx.x >> 5;
+  if (w < rows) {
+    const int kk = min(topk, nbk);
+    int64_t* dst = out_idx + ((long long)bh * nbq + bq0 + w) * kk;
+    warp_topk(keys + w * nbk, nbk, kk, hist[w], [&](int pos, int idx) { dst[pos] = idx; });
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -171,7 +242,7 @@ extern "C" int mi_block_pool_topk(mi_tensor4 q, mi_tensor4 k, int64_t B, int64_t
   if (B < 0 || H < 0 || S_q < 0 || S_k < 0 || D <= 0 || D > 128 || topk < 1) return MI_ERR_SHAPE;
   if (q.stride_d != 1 || k.stride_d != 1) return MI_ERR_SHAPE;
   const int64_t nbq = (S_q + 63) / 64, nbk = (S_k + 63) / 64;
-  if (nbk > kMaxBlocks || nbq > 65535) return MI_ERR_SHAPE;
+  if (nbk > kMaxBlocks || nbq > 65535 * kSelRows) return MI_ERR_SHAPE;
   if (B == 0 || H == 0 || nbq == 0) return MI_OK;
   if (nbk == 0) return MI_ERR_SHAPE;
   if (workspace_bytes < mi_block_pool_topk_workspace_size(B, H, S_q, S_k, D) || !workspace)
@@ -180,17 +251,37 @@ extern "C" int mi_block_pool_topk(mi_tensor4 q, mi_tensor4 k, int64_t B, int64_t
   float* q_pool = reinterpret_cast<float*>(workspace);
   float* k_poolT = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) +
                                             align_up(sizeof(float) * B * H * nbq * D));
-  dim3 g1((unsigned)max(nbq, nbk), (unsigned)H, (unsigned)B);
-  if (dtype == MI_BF16)
-    pool_kernel<__nv_bfloat16><<<g1, 256, 0, st>>>(q, k, (int)H, (int)S_q, (int)S_k, (int)D,
-                                                   (int)nbq, (int)nbk, q_pool, k_poolT);
-  else
-    pool_kernel<__half><<<g1, 256, 0, st>>>(q, k, (int)H, (int)S_q, (int)S_k, (int)D, (int)nbq,
-                                            (int)nbk, q_pool, k_poolT);
-  dim3 g2((unsigned)nbq, (unsigned)H, (unsigned)B);
-  block_select_kernel<<<g2, kSelThreads, 0, st>>>(q_pool, k_poolT, (int)H, (int)D, (int)nbq,
-                                                  (int)nbk, (int)topk, force_sink_diag,
-                                                  score_scale, out_idx);
+  const bool vec_ok = (D % 8 == 0) && !(reinterpret_cast<uintptr_t>(q.ptr) & 15) &&
+                      !(reinterpret_cast<uintptr_t>(k.ptr) & 15) && !(q.stride_s % 8) &&
+                      !(k.stride_s % 8) && !(q.stride_h % 8) && !(k.stride_h % 8) &&
+                      !(q.stride_b % 8) && !(k.stride_b % 8);
+  if (vec_ok) {
+    dim3 g1((unsigned)((max(nbq, nbk) + 7) / 8), (unsigned)H, (unsigned)(2 * B));
+    const int nthr = 8 * (int)(D / 8);
+    if (dtype == MI_BF16)
+      pool_kernel_v<__nv_bfloat16><<<g1, nthr, 0, st>>>(q, k, (int)H, (int)S_q, (int)S_k, (int)D,
+                                                        (int)nbq, (int)nbk, q_pool, k_poolT);
+    else
+      pool_kernel_v<__half><<<g1, nthr, 0, st>>>(q, k, (int)H, (int)S_q, (int)S_k, (int)D,
+                                                 (int)nbq, (int)nbk, q_pool, k_poolT);
+  } else {
+    dim3 g1((unsigned)max(nbq, nbk), (unsigned)H, (unsigned)B);
+    if (dtype == MI_BF16)
+      pool_kernel<__nv_bfloat16><<<g1, 256, 0, st>>>(q, k, (int)H, (int)S_q, (int)S_k, (int)D,
+                                                     (int)nbq, (int)nbk, q_pool, k_poolT);
+    else
+      pool_kernel<__half><<<g1, 256, 0, st>>>(q, k, (int)H, (int)S_q, (int)S_k, (int)D,
+                                              (int)nbq, (int)nbk, q_pool, k_poolT);
+  }
+  const size_t smem2 = (size_t)kSelRows * nbk * 4 + (size_t)kSelRows * D * 4;
+  if (smem2 > 200 * 1024) return MI_ERR_SHAPE;  // ~S > 400K tokens
+  if (cudaFuncSetAttribute(block_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem2) != cudaSuccess)
+    return MI_ERR_LAUNCH;
+  dim3 g2((unsigned)((nbq + kSelRows - 1) / kSelRows), (unsigned)H, (unsigned)B);
+  block_select_kernel<<<g2, kSelThreads, smem2, st>>>(q_pool, k_poolT, (int)H, (int)D, (int)nbq,
+                                                      (int)nbk, (int)topk, force_sink_diag,
+                                                      score_scale, out_idx);
   return cudaGetLastError() == cudaSuccess ? MI_OK : MI_ERR_LAUNCH;
 }
 

@@ -140,4 +140,77 @@ __device__ void block_topk(const uint32_t* keys, int n, int k, TopkSmem<NT>& sm,
   (void)lane;
 }
 
+// Warp-scope variant: the calling warp selects k of n keys on its own (no
+// block barriers), with `hist` a 256-int scratch private to the warp.  Lane l
+// reads indices l, l+32, ... (conflict-free in shared memory); index order
+// for the tie-break and the output comes from ballots over each group of 32
+// consecutive indices.  Same result as block_topk.
+template <typename Emit>
+__device__ void warp_topk(const uint32_t* keys, int n, int k, int* hist, Emit emit) {
+  const int lane = threadIdx.x & 31;
+  const unsigned lt = (1u << lane) - 1u;
+  if (k <= 0) return;
+  if (k > n) k = n;
+  uint32_t prefix = 0, pmask = 0;
+  int remaining = k;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) hist[lane * 8 + q] = 0;
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) {
+      const uint32_t key = keys[i];
+      if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1);
+    }
+    __syncwarp();
+    int c[8];
+    int s = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      c[q] = hist[255 - 8 * lane - q];
+      s += c[q];
+    }
+    int incl = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const int excl = incl - s;
+    const unsigned hit = __ballot_sync(0xffffffffu, incl >= remaining);
+    const int first = __ffs(hit) - 1;
+    int digit = 0, rem_new = 0;
+    if (lane == first) {
+      int cum = excl;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (cum + c[q] >= remaining) {
+          digit = 255 - 8 * lane - q;
+          rem_new = remaining - cum;
+          break;
+        }
+        cum += c[q];
+      }
+    }
+    digit = __shfl_sync(0xffffffffu, digit, first);
+    remaining = __shfl_sync(0xffffffffu, rem_new, first);
+    prefix |= (uint32_t)digit << shift;
+    pmask |= 255u << shift;
+    __syncwarp();
+  }
+  const uint32_t T = prefix;
+  int eq_seen = 0, pos = 0;
+  for (int base = 0; base < n; base += 32) {
+    const int i = base + lane;
+    const bool valid = i < n;
+    const uint32_t key = valid ? keys[i] : 0u;
+    const bool eq = valid && key == T;
+    const unsigned eqb = __ballot_sync(0xffffffffu, eq);
+    const bool sel = valid && (key > T || (eq && eq_seen + __popc(eqb & lt) < remaining));
+    const unsigned selb = __ballot_sync(0xffffffffu, sel);
+    if (sel) emit(pos + __popc(selb & lt), i);
+    pos += __popc(selb);
+    eq_seen += __popc(eqb);
+  }
+}
+
 }  // namespace mib200

@@ -45,7 +45,9 @@ class mi_tensor4(ctypes.Structure):
 
 
 def library_path() -> str:
-    return os.path.join(_HERE, _LIB_NAME)
+    # MINFERENCE_B200_LIB points at an alternative build of the same library
+    # (e.g. a tuning variant); by default the in-tree build is used.
+    return os.environ.get("MINFERENCE_B200_LIB") or os.path.join(_HERE, _LIB_NAME)
 
 
 def lib() -> ctypes.CDLL:
