@@ -24,8 +24,6 @@
  *                          index estimation)
  *   mi_vs_sparse_fwd      minference/ops/vertical_slash_kernel_npu.py:255-415
  *                         (_build_vs_mask_direct + _vertical_slash_pytorch_ref)
- *   mi_vs_convert_indexes minference/backend_npu/cuda_shim.py:147-236
- *                         (convert_vertical_slash_indexes, legacy format)
  */
 #ifndef MINFERENCE_B200_H_
 #define MINFERENCE_B200_H_
@@ -45,6 +43,7 @@ extern "C" {
 #define MI_ERR_LAUNCH 4      /* CUDA launch / driver error */
 #define MI_ERR_ALIGN 5       /* pointer or stride alignment not usable by TMA */
 #define MI_ERR_DEVICE 6      /* not an sm_100 device */
+#define MI_ERR_SCRATCH_LIMIT 7 /* problem needs more than the built-in scratch */
 
 /* Element types of q/k/v/out. */
 #define MI_F16 0
@@ -86,6 +85,25 @@ int mi_block_pool_topk(mi_tensor4 q, mi_tensor4 k, int64_t B, int64_t H, int64_t
                        int64_t S_k, int64_t D, int dtype, int64_t topk, int force_sink_diag,
                        float score_scale, int64_t* out_idx, void* workspace,
                        size_t workspace_bytes, void* stream);
+
+/* Allocation-free variant of mi_block_pool_topk.  No counterpart in the
+ * reference.  It is meant for callers that cannot allocate device memory when
+ * they call in -- code being captured into a CUDA graph, or engines that have
+ * given the whole device heap to their own pool -- so instead of taking a
+ * workspace it uses a fixed scratch array compiled into the library
+ * (mi_block_pool_topk_noalloc_limit() bytes, 32 MiB, held on every GPU that
+ * loads the library until the process exits).  Same arguments and results as
+ * mi_block_pool_topk without the workspace; returns MI_ERR_SCRATCH_LIMIT when
+ * mi_block_pool_topk_workspace_size(...) exceeds the limit.  The first call on
+ * each device looks up the array's device address (cudaGetSymbolAddress), so
+ * make that first call before any stream capture.  All calls share the one
+ * array: calls that overlap on the GPU race and must be serialised by the
+ * caller.  Allocates nothing (no cudaMalloc / cudaFree). */
+size_t mi_block_pool_topk_noalloc_limit(void);
+int mi_block_pool_topk_noalloc(mi_tensor4 q, mi_tensor4 k, int64_t B, int64_t H, int64_t S_q,
+                               int64_t S_k, int64_t D, int dtype, int64_t topk,
+                               int force_sink_diag, float score_scale, int64_t* out_idx,
+                               void* stream);
 
 /* block_sparse attention from per-query-block key-block lists:
  * block_idx int64 [B, H, ceil(S/64), topk] (any order, duplicates and

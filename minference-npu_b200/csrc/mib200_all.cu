@@ -4,3 +4,4 @@
 #include "attention.cu"
 #include "block_sparse.cu"
 #include "vs_index.cu"
+#include "noalloc.cu"

@@ -26,6 +26,7 @@ _STATUS = {
     4: "CUDA launch error",
     5: "pointer/stride alignment not usable by TMA (need 16-byte aligned rows)",
     6: "not an sm_100 device",
+    7: "problem larger than the library's built-in scratch (allocation-free entry point)",
 }
 MI_F16, MI_BF16 = 0, 1
 
