@@ -358,6 +358,69 @@ def run_reference_arm(args, rank, world) -> None:
     print(json.dumps(line), flush=True)
 
 
+def phi3_mini_config():
+    """Phi-3-mini-128k architecture (32 layers, hidden 3072, 32 heads of 96,
+    SwiGLU MLP 8192, RMSNorm, vocab 32064, LongRoPE 'su' scaling).  The
+    LongRoPE factors are seeded synthetic values (random init; no checkpoint)."""
+    from transformers import Phi3Config
+
+    g = np.random.default_rng(0)
+    short = (1.0 + 0.05 * np.sort(g.random(48))).tolist()
+    long_ = (1.0 + 60.0 * np.sort(g.random(48))).tolist()
+    return Phi3Config(
+        vocab_size=32064, hidden_size=3072, intermediate_size=8192, num_hidden_layers=32,
+        num_attention_heads=32, num_key_value_heads=32, max_position_embeddings=131072,
+        original_max_position_embeddings=4096, rms_norm_eps=1e-5, pad_token_id=32000,
+        rope_scaling={"type": "longrope", "short_factor": short, "long_factor": long_},
+        attn_implementation="sdpa",
+    )
+
+
+def run_ttft(args) -> None:
+    """time to first token (prefill + 1 output token) of a
+    random-init Phi-3-mini-128k at the given contexts, per attention type
+    (minference: per-head patterns from the seeded config; dense: every head
+    on this build's dense kernel; hf: unpatched transformers SDPA)."""
+    from transformers import Phi3ForCausalLM
+
+    from minference import MInference
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    ctxs = [int(c) for c in args.ctx.split(",")]
+    for attn_type in args.attn_types.split(","):
+        prev = torch.get_default_dtype()
+        torch.set_default_dtype(torch.bfloat16)
+        torch.manual_seed(0)
+        with torch.device(device):
+            model = Phi3ForCausalLM(phi3_mini_config()).eval()
+        torch.set_default_dtype(prev)
+        if attn_type != "hf":
+            model = MInference(attn_type, model_name="microsoft/Phi-3-mini-128k-instruct")(model)
+        for ctx in ctxs:
+            g = torch.Generator(device=device).manual_seed(ctx)
+            ids = torch.randint(0, 32064, (1, ctx), generator=g, device=device)
+            times = []
+            with torch.no_grad():
+                for it in range(1 + args.ttft_runs):
+                    torch.cuda.synchronize()
+                    a = torch.cuda.Event(enable_timing=True)
+                    b = torch.cuda.Event(enable_timing=True)
+                    a.record()
+                    logits = model(ids, logits_to_keep=1).logits
+                    tok = logits[:, -1].argmax(-1)
+                    b.record()
+                    torch.cuda.synchronize()
+                    if it > 0:
+                        times.append(a.elapsed_time(b) / 1e3)
+            print(json.dumps({"metric": "phi3_mini_128k_ttft", "attn_type": attn_type, "ctx": ctx,
+                              "ttft_s": statistics.median(times), "runs": len(times),
+                              "first_token": int(tok.item()), "dtype": "bf16",
+                              "data": "random-init weights, uniform token ids"}), flush=True)
+        del model
+        torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -370,6 +433,11 @@ def main():
                     choices=["mixed", "vertical_and_slash", "block_sparse", "stream_llm", "dense"],
                     help="all heads use one pattern (profiling / per-pattern numbers)")
     ap.add_argument("--heads", type=int, default=H_TOTAL)
+    ap.add_argument("--ttft", action="store_true",
+                    help="time to first token of a random-init Phi-3-mini-128k (config 3)")
+    ap.add_argument("--ctx", default="4096,8192,16384,32768,65536")
+    ap.add_argument("--attn-types", default="minference,dense,hf")
+    ap.add_argument("--ttft-runs", type=int, default=2)
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -378,6 +446,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
+        return
+    if args.ttft:
+        run_ttft(args)
         return
     assert args.heads % world == 0, "heads must divide evenly over ranks"
     torch.cuda.set_device(local_rank)

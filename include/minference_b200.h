@@ -24,6 +24,8 @@
  *                          index estimation)
  *   mi_vs_sparse_fwd      minference/ops/vertical_slash_kernel_npu.py:255-415
  *                         (_build_vs_mask_direct + _vertical_slash_pytorch_ref)
+ *   mi_vs_convert_indexes minference/backend_npu/cuda_shim.py:147-236
+ *                         (convert_vertical_slash_indexes, legacy format)
  */
 #ifndef MINFERENCE_B200_H_
 #define MINFERENCE_B200_H_
@@ -141,6 +143,20 @@ int mi_vs_sparse_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor4 out, i
                      int64_t H, int64_t S, int64_t D, int dtype, const int32_t* v_idx,
                      int64_t nv, const int32_t* s_idx, int64_t ns, float softmax_scale,
                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* Legacy four-array VS index format of upstream MInference, as restated by
+ * the reference's CPU port convert_vertical_slash_indexes
+ * (minference/backend_npu/cuda_shim.py:147-236): per (b, h, 64-row query
+ * block) the slash ranges as 64-key block offsets (merged with the upstream
+ * one-block extension rule) and the vertical columns not covered by them.
+ * seqlens int32 [B]; v_idx int32 [B,H,nv] ascending; s_idx int32 [B,H,ns]
+ * descending.  Outputs (int32, fully written): block_count [B,H,R],
+ * block_offset [B,H,R,ns], column_count [B,H,R], column_index [B,H,R,nv],
+ * R = ceil(context_size/64). */
+int mi_vs_convert_indexes(const int32_t* seqlens, const int32_t* v_idx, int64_t nv,
+                          const int32_t* s_idx, int64_t ns, int64_t B, int64_t H,
+                          int64_t context_size, int32_t* block_count, int32_t* block_offset,
+                          int32_t* column_count, int32_t* column_index, void* stream);
 
 #ifdef __cplusplus
 }

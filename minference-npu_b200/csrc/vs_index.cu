@@ -470,3 +470,115 @@ extern "C" int mi_vs_sparse_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_ten
   prm.plan_head_stride = head_stride;
   return launch_attention(q, k, v, out, D, dtype, prm, st);
 }
+
+// ---------------------------------------------------------------------------
+// Legacy four-array VS index format (upstream MInference's
+// convert_vertical_slash_indexes; the reference's CPU port is
+// minference/backend_npu/cuda_shim.py:53-236).  One thread per
+// (b, h, 64-row query block) runs the two-pointer merge of the ascending
+// vertical list and the descending slash list:
+//   * slashes s >= end_m are skipped;
+//   * each slash gives a range ending at max(end_m - s, 64); a range that
+//     starts more than one block after the current one is flushed as 64-key
+//     blocks, a touching/overlapping one extends the current range by exactly
+//     one block (the upstream "+= blk" rule, a superset of the exact union);
+//   * vertical columns before the current range start are kept as columns;
+//     columns inside a range are dropped; with no valid slash every vertical
+//     column < end_m is kept.
+// Rows past seqlens[b] get zero counts.  Entries beyond the counts are zero.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) vs_convert_kernel(
+    const int32_t* seqlens, const int32_t* v_idx, int nv, const int32_t* s_idx, int ns, int H,
+    int num_rows, int32_t* block_count, int32_t* block_offset, int32_t* column_count,
+    int32_t* column_index) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  const int h = blockIdx.y, b = blockIdx.z, bh = b * H + h;
+  if (row >= num_rows) return;
+  const long long ro = (long long)bh * num_rows + row;
+  int32_t* boff = block_offset + ro * ns;
+  int32_t* cidx = column_index + ro * nv;
+  const int32_t* vl = v_idx + (long long)bh * nv;
+  const int32_t* sl = s_idx + (long long)bh * ns;
+  const int blk = 64;
+  const int start_m = row * blk;
+  int nb = 0, nc = 0;
+  if (start_m < seqlens[b]) {
+    const int end_m = start_m + blk;
+    int v = 0, s = 0;
+    int v_val;
+    if (nv == 0) {
+      v_val = end_m + blk;
+    } else {
+      v_val = vl[0];
+      v = 1;
+    }
+    int s_raw = 0;
+    bool found = false;
+    while (s < ns) {
+      s_raw = sl[s++];
+      if (s_raw < end_m) {
+        found = true;
+        break;
+      }
+    }
+    if (!found) {
+      while (true) {
+        if (v_val <= end_m + blk && v_val < end_m) cidx[nc++] = v_val;
+        if (v < nv) {
+          v_val = vl[v++];
+        } else {
+          break;
+        }
+      }
+    } else {
+      int range_end = max(end_m - s_raw, blk);
+      int range_start = range_end - blk;
+      while (true) {
+        if (v_val < range_end) {
+          if (v_val < range_start) cidx[nc++] = v_val;
+          if (v < nv) {
+            v_val = vl[v++];
+          } else {
+            v_val = end_m + blk;
+          }
+        } else {
+          int new_end;
+          if (s < ns) {
+            new_end = max(end_m - sl[s++], blk);
+          } else {
+            for (int x = range_start; x < range_end; x += blk) boff[nb++] = x;
+            break;
+          }
+          if (new_end > range_end + blk) {
+            for (int x = range_start; x < range_end; x += blk) boff[nb++] = x;
+            range_start = new_end - blk;
+            range_end = new_end;
+          } else if (new_end > range_end) {
+            range_end += blk;
+          }
+        }
+      }
+    }
+  }
+  block_count[ro] = nb;
+  column_count[ro] = nc;
+  for (int i = nb; i < ns; ++i) boff[i] = 0;
+  for (int i = nc; i < nv; ++i) cidx[i] = 0;
+}
+
+extern "C" int mi_vs_convert_indexes(const int32_t* seqlens, const int32_t* v_idx, int64_t nv,
+                                     const int32_t* s_idx, int64_t ns, int64_t B, int64_t H,
+                                     int64_t context_size, int32_t* block_count,
+                                     int32_t* block_offset, int32_t* column_count,
+                                     int32_t* column_index, void* stream) {
+  if (B < 0 || H < 0 || nv < 0 || ns < 0 || context_size < 0 || context_size > (1ll << 30))
+    return MI_ERR_SHAPE;
+  if (B > 65535 || H > 65535) return MI_ERR_SHAPE;
+  const int64_t num_rows = (context_size + 63) / 64;
+  if (B == 0 || H == 0 || num_rows == 0) return MI_OK;
+  dim3 g((unsigned)((num_rows + 127) / 128), (unsigned)H, (unsigned)B);
+  vs_convert_kernel<<<g, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      seqlens, v_idx, (int)nv, s_idx, (int)ns, (int)H, (int)num_rows, block_count, block_offset,
+      column_count, column_index);
+  return cudaGetLastError() == cudaSuccess ? MI_OK : MI_ERR_LAUNCH;
+}

@@ -89,6 +89,8 @@ def lib() -> ctypes.CDLL:
         L.mi_vs_sparse_fwd_workspace_size.restype = SZ
         L.mi_vs_sparse_fwd.argtypes = [T4, T4, T4, T4, I64, I64, I64, I64, I, P, I64, P, I64, F, P, SZ, P]
         L.mi_vs_sparse_fwd.restype = I
+        L.mi_vs_convert_indexes.argtypes = [P, P, I64, P, I64, I64, I64, I64, P, P, P, P, P]
+        L.mi_vs_convert_indexes.restype = I
         _lib = L
     return _lib
 

@@ -7,6 +7,7 @@ from .block_sparse import (
 )
 from .streaming import dense_attention, streaming_forward
 from .vertical_slash import (
+    convert_vertical_slash_indexes,
     vertical_and_slash,
     vertical_and_slash_estimate,
     vertical_slash_sparse_attention,
@@ -21,4 +22,5 @@ __all__ = [
     "vertical_and_slash",
     "vertical_and_slash_estimate",
     "vertical_slash_sparse_attention",
+    "convert_vertical_slash_indexes",
 ]

@@ -18,7 +18,12 @@ from .. import _native
 from ._common import check_qkv, default_softmax_scale, kernel_dim, prepare
 from ._common import output as _common_out
 
-__all__ = ["vertical_slash_sparse_attention", "vertical_and_slash_estimate", "vertical_and_slash"]
+__all__ = [
+    "vertical_slash_sparse_attention",
+    "vertical_and_slash_estimate",
+    "vertical_and_slash",
+    "convert_vertical_slash_indexes",
+]
 
 LAST_Q = 64
 
@@ -82,3 +87,39 @@ def vertical_and_slash(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, vertic
     """Estimate indices from the last 64 queries, then run the sparse attention."""
     v_idx, s_idx = vertical_and_slash_estimate(q, k, vertical_size, slash_size)
     return vertical_slash_sparse_attention(q, k, v, v_idx, s_idx, out=out)
+
+
+def convert_vertical_slash_indexes(seqlens: torch.Tensor, vertical_indexes: torch.Tensor,
+                                   slash_indexes: torch.Tensor, context_size: int,
+                                   block_size_M: int = 64, block_size_N: int = 64,
+                                   causal: bool = True):
+    """Legacy four-array index format of upstream MInference.
+
+    Same signature and results as the reference's CPU port
+    (MInference-NPU minference/backend_npu/cuda_shim.py:147-236), computed on
+    the GPU (one thread per query block): returns ``(block_count [B,H,R],
+    block_offset [B,H,R,NNZ_S], column_count [B,H,R], column_index
+    [B,H,R,NNZ_V])`` as int32 CUDA tensors, R = ceil(context_size / 64)."""
+    if block_size_M != 64 or block_size_N != 64:
+        raise AssertionError("block_size_M / block_size_N must be 64")
+    if not causal:
+        raise NotImplementedError("only causal=True is supported")
+    dev = slash_indexes.device
+    _native.require_cuda(slash_indexes)
+    B, H, ns = slash_indexes.shape
+    nv = vertical_indexes.shape[2]
+    vi = vertical_indexes.to(device=dev, dtype=torch.int32).contiguous()
+    si = slash_indexes.to(device=dev, dtype=torch.int32).contiguous()
+    sl = seqlens.to(device=dev, dtype=torch.int32).contiguous()
+    R = -(-int(context_size) // 64)
+    bc = torch.empty((B, H, R), dtype=torch.int32, device=dev)
+    bo = torch.empty((B, H, R, ns), dtype=torch.int32, device=dev)
+    cc = torch.empty((B, H, R), dtype=torch.int32, device=dev)
+    ci = torch.empty((B, H, R, nv), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        rc = _native.lib().mi_vs_convert_indexes(
+            sl.data_ptr(), vi.data_ptr(), nv, si.data_ptr(), ns, B, H, int(context_size),
+            bc.data_ptr(), bo.data_ptr(), cc.data_ptr(), ci.data_ptr(), _native.stream_ptr(dev),
+        )
+    _native.check(rc, "mi_vs_convert_indexes")
+    return bc, bo, cc, ci

@@ -14,6 +14,7 @@ functions followed (paths relative to the MInference-NPU project root):
 * ``stream_mask``          streaming_kernel_npu.py:94-146 (visible set at :131-136)
 * ``vs_estimate``          minference_forward.py:124-167
 * ``vs_mask``              vertical_slash_kernel_npu.py:255-369
+* ``vs_convert_indexes``   backend_npu/cuda_shim.py:147-236 (legacy format)
 * ``masked_attention``     block_sparse_kernel_npu.py:325-348,
                            vertical_slash_kernel_npu.py:377-415 (fp32 softmax,
                            fully masked rows -> 0)
@@ -54,6 +55,8 @@ def lib():
         L.oracle_vs_estimate.restype = i32
         L.oracle_vs_block_row.argtypes = [P, i32, P, i32, i32, i32, P]
         L.oracle_vs_block_row.restype = None
+        L.oracle_vs_convert_indexes.argtypes = [P, i32, P, i32, i32, i32, P, P, P, P]
+        L.oracle_vs_convert_indexes.restype = None
         L.oracle_det_exp.argtypes = [f32]
         L.oracle_det_exp.restype = f32
         _lib = L
@@ -128,6 +131,32 @@ def vs_estimate(q, k, vertical_size: int, slash_size: int, logit_scale: float | 
     if return_logits:
         return v_idx, s_idx, logits
     return v_idx, s_idx
+
+
+def vs_convert_indexes(seqlens, v_idx: np.ndarray, s_idx: np.ndarray, context_size: int):
+    """Legacy (block_count, block_offset, column_count, column_index), int32,
+    for v_idx [B,H,nv] ascending and s_idx [B,H,ns] descending."""
+    v_idx = np.ascontiguousarray(v_idx, dtype=np.int32)
+    s_idx = np.ascontiguousarray(s_idx, dtype=np.int32)
+    B, H, nv = v_idx.shape
+    ns = s_idx.shape[2]
+    R = -(-int(context_size) // 64)
+    bc = np.zeros((B, H, R), np.int32)
+    bo = np.zeros((B, H, R, ns), np.int32)
+    cc = np.zeros((B, H, R), np.int32)
+    ci = np.zeros((B, H, R, nv), np.int32)
+    for b in range(B):
+        for h in range(H):
+            v = np.ascontiguousarray(v_idx[b, h])
+            s = np.ascontiguousarray(s_idx[b, h])
+            o_bc = np.zeros(R, np.int32)
+            o_bo = np.zeros((R, ns), np.int32)
+            o_cc = np.zeros(R, np.int32)
+            o_ci = np.zeros((R, nv), np.int32)
+            lib().oracle_vs_convert_indexes(_ptr(v), nv, _ptr(s), ns, int(seqlens[b]), R,
+                                            _ptr(o_bc), _ptr(o_bo), _ptr(o_cc), _ptr(o_ci))
+            bc[b, h], bo[b, h], cc[b, h], ci[b, h] = o_bc, o_bo, o_cc, o_ci
+    return bc, bo, cc, ci
 
 
 def det_exp(y: float) -> float:

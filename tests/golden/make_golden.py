@@ -80,6 +80,29 @@ def pad128(t):
     return F.pad(t, (0, 128 - t.shape[-1])) if t.shape[-1] < 128 else t
 
 
+def make_convert_fixture() -> None:
+    """convert_vertical_slash_indexes (backend_npu/cuda_shim.py:147) golden vectors."""
+    _load_ref_package()
+    shim = importlib.import_module("ref_minference.backend_npu.cuda_shim")
+    g = torch.Generator().manual_seed(51)
+    out = {}
+    ccases = [(1, 2, 200, 10, 20, 200), (2, 2, 300, 25, 40, 260), (1, 3, 1000, 64, 80, 1000),
+              (1, 1, 130, 0, 12, 130), (1, 1, 190, 9, 0, 190)]
+    for ci, (B, H, S, nv, ns, seqlen) in enumerate(ccases):
+        v_idx = torch.stack([torch.stack([torch.randperm(S, generator=g)[:nv].sort().values
+                                          for _ in range(H)]) for _ in range(B)]).to(torch.int32)
+        s_idx = torch.stack([torch.stack([torch.randperm(S, generator=g)[:ns].sort(descending=True).values
+                                          for _ in range(H)]) for _ in range(B)]).to(torch.int32)
+        seqlens = torch.full((B,), seqlen, dtype=torch.int32)
+        bc, bo, cc, cix = shim.convert_vertical_slash_indexes(seqlens, v_idx, s_idx, S, 64, 64)
+        out[f"c{ci}_meta"] = np.array([B, H, S, nv, ns, seqlen])
+        out[f"c{ci}_vidx"], out[f"c{ci}_sidx"] = v_idx.numpy(), s_idx.numpy()
+        out[f"c{ci}_bc"], out[f"c{ci}_bo"] = bc.numpy(), bo.numpy()
+        out[f"c{ci}_cc"], out[f"c{ci}_ci"] = cc.numpy(), cix.numpy()
+    out["n_cases"] = np.array(len(ccases))
+    np.savez_compressed(os.path.join(HERE, "vs_convert.npz"), **out)
+
+
 def main() -> None:
     bs, st, vs, fw = _load_ref_package()
     torch.set_num_threads(min(8, os.cpu_count() or 1))
@@ -216,8 +239,12 @@ def main() -> None:
         out[f"c{ci}_visible"] = np.packbits((~mask).numpy(), axis=-1)
     out["n_cases"] = np.array(len(mcases))
     np.savez_compressed(os.path.join(HERE, "vs_mask.npz"), **out)
+    make_convert_fixture()
     print("golden fixtures written to", HERE)
 
 
 if __name__ == "__main__":
-    main()
+    if "--only-convert" in sys.argv:
+        make_convert_fixture()
+    else:
+        main()

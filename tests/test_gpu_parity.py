@@ -301,3 +301,35 @@ def test_device_error_word_clear(cuda):
     from minference import _native
 
     assert _native.device_error() == 0
+
+
+# ---------------------------------------------------------------------------
+# legacy VS index format
+# ---------------------------------------------------------------------------
+def test_vs_convert_golden(cuda):
+    from minference.backend_npu import convert_vertical_slash_indexes
+
+    z = golden("vs_convert.npz")
+    for ci in range(int(z["n_cases"])):
+        B, H, S, nv, ns, seqlen = [int(x) for x in z[f"c{ci}_meta"]]
+        got = convert_vertical_slash_indexes(
+            torch.full((B,), seqlen, dtype=torch.int32), torch.from_numpy(z[f"c{ci}_vidx"]).to(cuda),
+            torch.from_numpy(z[f"c{ci}_sidx"]).to(cuda), S, 64, 64)
+        for arr, name in zip(got, ("bc", "bo", "cc", "ci")):
+            assert np.array_equal(arr.cpu().numpy(), z[f"c{ci}_{name}"]), f"case {ci} {name}"
+
+
+@pytest.mark.parametrize("S,nv,ns,seqlen", [(4096, 1000, 1500, 4096), (8192, 300, 2000, 7000),
+                                            (1000, 64, 0, 1000), (3000, 0, 200, 3000)])
+def test_vs_convert_bit_exact(cuda, S, nv, ns, seqlen):
+    from minference.ops import convert_vertical_slash_indexes
+
+    O = _oracle()
+    g = torch.Generator().manual_seed(S + nv)
+    v = torch.stack([torch.randperm(S, generator=g)[:nv].sort().values for _ in range(3)])[None].int()
+    s = torch.stack([torch.randperm(S, generator=g)[:ns].sort(descending=True).values
+                     for _ in range(3)])[None].int()
+    got = convert_vertical_slash_indexes(torch.tensor([seqlen]), v.to(cuda), s.to(cuda), S)
+    ref = O.vs_convert_indexes([seqlen], v.numpy(), s.numpy(), S)
+    for a, r in zip(got, ref):
+        assert np.array_equal(a.cpu().numpy(), r)

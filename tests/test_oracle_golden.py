@@ -140,3 +140,13 @@ def test_det_exp_accuracy(y):
     got = O.det_exp(y)
     want = math.exp(y) if y >= -87.0 else 0.0
     assert got == pytest.approx(want, rel=4e-7, abs=1e-37)
+
+
+def test_vs_convert_indexes_matches_reference():
+    O = _oracle()
+    z = golden("vs_convert.npz")
+    for ci in range(int(z["n_cases"])):
+        B, H, S, nv, ns, seqlen = [int(x) for x in z[f"c{ci}_meta"]]
+        got = O.vs_convert_indexes([seqlen] * B, z[f"c{ci}_vidx"], z[f"c{ci}_sidx"], S)
+        for arr, name in zip(got, ("bc", "bo", "cc", "ci")):
+            assert np.array_equal(arr, z[f"c{ci}_{name}"]), f"case {ci} {name}"
