@@ -5,28 +5,6 @@
 
 namespace mib200 {
 
-// Tuning knobs (compile-time):
-//   MI_POLY_MASK   pair index c uses the FMA-pipe exp2 when (c & MI_POLY_MASK) == MI_POLY_MASK
-//                  (3: one pair in four, 1: one in two)
-//   MI_PACK_INT    1: round P to 16 bits with integer ops + byte permute (ALU pipe)
-//                  instead of the cvt.rn.bf16x2 conversion
-#ifndef MI_POLY_MASK
-#define MI_POLY_MASK 3
-#endif
-#ifndef MI_PACK_INT
-#define MI_PACK_INT 0
-#endif
-
-// bf16x2 from two non-negative floats: round half up on the dropped 16 bits,
-// then keep the high halves (one PRMT).  Used for P (values in [0, 256]).
-__device__ __forceinline__ uint32_t pack_bf16_int(float a, float b) {
-  const uint32_t ua = __float_as_uint(a) + 0x8000u;
-  const uint32_t ub = __float_as_uint(b) + 0x8000u;
-  uint32_t r;
-  asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(r) : "r"(ua), "r"(ub));
-  return r;
-}
-
 // Softmax of one 64-key block for one query row, in registers.
 // s: raw scores (overwritten).  Returns the block max of raw visible scores.
 struct RowState {
@@ -113,8 +91,18 @@ __global__ void __launch_bounds__(kThreads, 2)
     *abort_flag = 0;
     fence_barrier_init();
   }
+  // Constant chunk NC of every V stage: column 0 = 1, other columns 0 (64-byte
+  // swizzled like the TMA-loaded chunks).  TMA never writes it.
+  for (int i = threadIdx.x; i < kVStages * kBN * 4; i += kThreads) {
+    const int st = i / (kBN * 4), r = (i >> 2) % kBN, lu = i & 3;
+    const uint16_t one = DType<DT>::kBF16 ? (uint16_t)0x3F80 : (uint16_t)0x3C00;
+    const uint4 val = make_uint4(lu == 0 ? (uint32_t)one : 0u, 0u, 0u, 0u);
+    *reinterpret_cast<uint4*>(smem + L::kVOff + st * L::kVBytes + NC * (kBN * 64) + r * 64 +
+                              ((lu ^ ((r >> 1) & 3)) << 4)) = val;
+  }
+  fence_proxy_async_smem();
   if (warp == 5) {
-    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_alloc(tmem_slot, L::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -151,7 +139,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         int kb;
         uint64_t m0, m1;
         src.get(j, kb, m0, m1);
-        uint8_t* dst = smem + L::kVOff + st * L::kKVBytes;
+        uint8_t* dst = smem + L::kVOff + st * L::kVBytes;
         mbar_arrive_expect_tx(&v_full[st], L::kKVBytes);
         for (int c = 0; c < NC; ++c)
           tma_load_4d(dst + c * (kBN * 64), &tm_v, &v_full[st], c * 32, kb * kBN, h, b);
@@ -170,7 +158,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ======================= MMA issuer =======================================
     if (lane == 0) {
       constexpr uint32_t idesc_qk = make_idesc_f16(kBF16, kBM, kBN, false, false);
-      constexpr uint32_t idesc_pv = make_idesc_f16(kBF16, kBM, D, false, true);
+      constexpr uint32_t idesc_pv = make_idesc_f16(kBF16, kBM, L::kOCols, false, true);
       const uint32_t sq = smem_u32(smem + L::kQOff);
       const uint32_t sk0 = smem_u32(smem + L::kKOff);
       const uint32_t sv0 = smem_u32(smem + L::kVOff);
@@ -204,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int st = j % kVStages;
         if (!mbar_wait(&v_full[st], (j / kVStages) & 1, 106)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sv = sv0 + st * L::kKVBytes;
+        const uint32_t sv = sv0 + st * L::kVBytes;
         const uint32_t tmem_p = tmem_base + (j & 1) * kBN;
 #pragma unroll
         for (int ks = 0; ks < kBN / 16; ++ks) {
@@ -224,7 +212,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     const float NEG_INF = -INFINITY;
     const float sc = p.scale_log2;
     float m_used = NEG_INF;
-    float l = 0.f;
     bool ok = true;
 
     int kb_n = 0;
@@ -241,10 +228,19 @@ __global__ void __launch_bounds__(kThreads, 2)
       const long long key0 = (long long)kb * kBN;
       // Visible keys of this row inside the block:
       //   mask AND key <= a AND key < Sk AND (key < n_init OR key > a - n_local).
-      const uint64_t vis = mask & bits_below(a - key0 + 1) & bits_below((long long)p.Sk - key0) &
-                           (bits_below(p.n_init - key0) | ~bits_below(a - p.n_local - key0 + 1));
-      const bool all_full = __all_sync(0xffffffffu, vis == ~0ull);
-      const bool all_empty = __all_sync(0xffffffffu, vis == 0ull);
+      // Warp-uniform shortcut for blocks wholly visible to the warp's 32 rows.
+      const long long a_w0 = a - lane, a_w1 = a - lane + 31;
+      const bool fast_full = (mask == ~0ull) && key0 + kBN - 1 <= a_w0 &&
+                             key0 + kBN - 1 < p.Sk &&
+                             (key0 > a_w1 - p.n_local || key0 + kBN - 1 < p.n_init);
+      uint64_t vis = ~0ull;
+      bool all_full = true, all_empty = false;
+      if (!fast_full) {
+        vis = mask & bits_below(a - key0 + 1) & bits_below((long long)p.Sk - key0) &
+              (bits_below(p.n_init - key0) | ~bits_below(a - p.n_local - key0 + 1));
+        all_full = __all_sync(0xffffffffu, vis == ~0ull);
+        all_empty = __all_sync(0xffffffffu, vis == 0ull);
+      }
       const uint32_t tmem_s = lane_base + (j & 1) * kBN;
 
       float s[kBN];
@@ -280,62 +276,33 @@ __global__ void __launch_bounds__(kThreads, 2)
         tc_fence_after();
         const float f = need ? ((m_used == NEG_INF) ? 0.f : fast_exp2(m_used - m_new)) : 1.f;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          float o[32];
-          tmem_ld32(lane_base + 128 + c * 32, o);
+        for (int c = 0; c < L::kOCols / 16; ++c) {
+          float o[16];
+          tmem_ld16(lane_base + 128 + c * 16, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int x = 0; x < 32; ++x) o[x] *= f;
-          tmem_st32(lane_base + 128 + c * 32, o);
+          for (int x = 0; x < 16; ++x) o[x] *= f;
+          tmem_st16(lane_base + 128 + c * 16, o);
         }
         tmem_wait_st();
-        if (need) {
-          l *= f;
-          m_used = m_new;
-        }
+        if (need) m_used = m_new;
       }
       // P = 2^(s*scale_log2 - m_used); rows with nothing visible yet keep P = 0.
+      // The row sums of P come out of the PV MMA (column D of O).
       uint32_t pk[kBN / 2];
-      float ls0 = 0.f, ls1 = 0.f;
       if (all_empty || m_used == NEG_INF) {
 #pragma unroll
         for (int c = 0; c < kBN / 2; ++c) pk[c] = 0u;
       } else {
         const uint64_t sc2 = pk2(sc, sc);
         const uint64_t nm2 = pk2(-m_used, -m_used);
-        uint64_t acc0 = pk2(0.f, 0.f), acc1 = pk2(0.f, 0.f);
 #pragma unroll
         for (int c = 0; c < kBN / 2; ++c) {
-          const uint64_t x2 = ffma2(pk2(s[2 * c], s[2 * c + 1]), sc2, nm2);
-          float p0, p1;
-          if (all_full && (c & MI_POLY_MASK) == MI_POLY_MASK) {  // share of pairs on the FMA pipe
-            float x0, x1;
-            upk2(x2, x0, x1);
-            poly_exp2x2(pk2(fmaxf(x0, -127.f), fmaxf(x1, -127.f)), p0, p1);
-          } else {
-            float x0, x1;
-            upk2(x2, x0, x1);
-            p0 = fast_exp2(x0);
-            p1 = fast_exp2(x1);
-          }
-          if (c & 1)
-            acc1 = fadd2(acc1, pk2(p0, p1));
-          else
-            acc0 = fadd2(acc0, pk2(p0, p1));
-#if MI_PACK_INT
-          if constexpr (kBF16) {
-            pk[c] = pack_bf16_int(p0, p1);
-          } else {
-            pk[c] = DType<DT>::pack2(p0, p1);
-          }
-#else
-          pk[c] = DType<DT>::pack2(p0, p1);
-#endif
+          float x0, x1;
+          upk2(ffma2(pk2(s[2 * c], s[2 * c + 1]), sc2, nm2), x0, x1);
+          pk[c] = DType<DT>::pack2(fast_exp2(x0), fast_exp2(x1));
         }
-        acc0 = fadd2(acc0, acc1);
-        upk2(acc0, ls0, ls1);
       }
-      l += ls0 + ls1;
       // P(j) overwrites the first 32 columns of S buffer (j & 1).
       tmem_st32u(tmem_s, pk);
       tmem_wait_st();
@@ -347,6 +314,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (!ok) *abort_flag = 1;
     bool have_o = false;
     float o[D];
+    float l = 0.f;
     if (ok && n_entries > 0) {
       const int jl = n_entries - 1;
       if (mbar_wait(&pv_done[jl & 1], (jl >> 1) & 1, 109)) {
@@ -354,7 +322,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int c = 0; c < D / 32; ++c)
           tmem_ld32(lane_base + 128 + c * 32, *reinterpret_cast<float(*)[32]>(&o[c * 32]));
+        float lc[16];
+        tmem_ld16(lane_base + 128 + D, lc);
         tmem_wait_ld();
+        l = lc[0];
         have_o = true;
       } else {
         ok = false;
@@ -393,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   if (warp == 5) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc(tmem_base, L::kTmemCols);
   }
 }
 

@@ -66,20 +66,25 @@ struct AttnParams {
 
 constexpr int kBM = 128;       // query rows per CTA
 constexpr int kBN = 64;        // keys per KV block
-constexpr int kKStages = 4;    // K ring depth (K runs ahead of V)
+constexpr int kKStages = 3;    // K ring depth (K runs ahead of V)
 constexpr int kVStages = 3;    // V ring depth
 constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 256;  // S0 [0,64), S1 [64,128), O [128,128+D); P(j) aliases S(j&1)
 
 template <int D>
 struct AttnSmem {
   static constexpr int NC = D / 32;                 // 64-byte chunks per row
   static constexpr int kQBytes = NC * kBM * 64;     // Q tile (reused for the output tile)
-  static constexpr int kKVBytes = NC * kBN * 64;    // one K (or V) block
+  static constexpr int kKVBytes = NC * kBN * 64;    // one K block (and the loaded part of V)
+  // A V stage holds NC loaded chunks plus one constant chunk whose first column
+  // is all ones: O += P V then also produces the row sums of P in O column D.
+  static constexpr int kVBytes = (NC + 1) * kBN * 64;
+  static constexpr int kOCols = D + 16;             // O columns incl. the row-sum column
+  // TMEM: S0 [0,64), S1 [64,128), O [128, 128+kOCols); P(j) aliases S(j&1)
+  static constexpr uint32_t kTmemCols = (128 + kOCols <= 256) ? 256u : 512u;
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kQOff + kQBytes;
   static constexpr int kVOff = kKOff + kKStages * kKVBytes;
-  static constexpr int kBarOff = kVOff + kVStages * kKVBytes;
+  static constexpr int kBarOff = kVOff + kVStages * kVBytes;
   // barriers: q_full, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
   //           s_full[2], p_full[2], pv_done[2]
   static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 6;

@@ -82,10 +82,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait for the completion of the phase with the given parity.
 // Returns false (and records `code`) if the limit is reached.
+#ifndef MI_SPIN_TEST
+#define MI_SPIN_TEST 0
+#endif
+__device__ __forceinline__ bool mbar_test_wait_p(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+#if MI_SPIN_TEST
+  // Pure polling: the waiting thread never suspends, so it observes the phase
+  // flip as soon as it happens.
+  for (uint32_t i = 0; i < 16u * kSpinLimit; ++i) {
+    if (mbar_test_wait_p(bar, parity)) return true;
+  }
+#else
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
   }
+#endif
   record_error(code);
   return false;
 }
