@@ -5,6 +5,48 @@
 
 namespace mib200 {
 
+// Exponential of the P tile (compile-time choice, measured in bench.py runs):
+//   MI_EXP_MODE 0: ex2.approx.f32 on the MUFU unit for every element
+//               1: bf16 only: x rounded to bf16 pairs, one ex2.approx.ftz.bf16x2 per pair
+//                  (half the MUFU operations; P comes out packed)
+//               2: as 0, but one pair in four on the FMA pipe (poly_exp2x2)
+//   MI_PACK_INT 1: bf16 P packed with integer rounding + PRMT (ALU) instead of the
+//                  cvt.rn.bf16x2 conversion, which shares the XU pipe with MUFU
+//   MI_POLY_EVERY  with mode 2: pair c uses the polynomial when c % MI_POLY_EVERY == MI_POLY_EVERY-1
+#ifndef MI_PACK_INT
+#define MI_PACK_INT 0
+#endif
+#ifndef MI_POLY_EVERY
+#define MI_POLY_EVERY 4
+#endif
+#ifndef MI_EXP_MODE
+#define MI_EXP_MODE 0
+#endif
+
+__device__ __forceinline__ uint32_t ex2_bf16x2(uint32_t x) {
+  uint32_t r;
+  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(r) : "r"(x));
+  return r;
+}
+
+// bf16x2 from two non-negative floats: round half up on the dropped 16 bits,
+// keep the high halves (one PRMT).  For P values in [0, 256].
+__device__ __forceinline__ uint32_t pack_bf16_int(float a, float b) {
+  const uint32_t ua = __float_as_uint(a) + 0x8000u;
+  const uint32_t ub = __float_as_uint(b) + 0x8000u;
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(r) : "r"(ua), "r"(ub));
+  return r;
+}
+
+template <typename DT>
+__device__ __forceinline__ uint32_t pack_p(float a, float b) {
+#if MI_PACK_INT
+  if constexpr (DType<DT>::kBF16) return pack_bf16_int(a, b);
+#endif
+  return DType<DT>::pack2(a, b);
+}
+
 // Softmax of one 64-key block for one query row, in registers.
 // s: raw scores (overwritten).  Returns the block max of raw visible scores.
 struct RowState {
@@ -300,7 +342,20 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int c = 0; c < kBN / 2; ++c) {
           float x0, x1;
           upk2(ffma2(pk2(s[2 * c], s[2 * c + 1]), sc2, nm2), x0, x1);
-          pk[c] = DType<DT>::pack2(fast_exp2(x0), fast_exp2(x1));
+#if MI_EXP_MODE == 1
+          if constexpr (kBF16) {
+            pk[c] = ex2_bf16x2(DType<DT>::pack2(x0, x1));
+            continue;
+          }
+#elif MI_EXP_MODE == 2
+          if (all_full && (c % MI_POLY_EVERY) == MI_POLY_EVERY - 1) {
+            float p0, p1;
+            poly_exp2x2(pk2(fmaxf(x0, -127.f), fmaxf(x1, -127.f)), p0, p1);
+            pk[c] = pack_p<DT>(p0, p1);
+            continue;
+          }
+#endif
+          pk[c] = pack_p<DT>(fast_exp2(x0), fast_exp2(x1));
         }
       }
       // P(j) overwrites the first 32 columns of S buffer (j & 1).
