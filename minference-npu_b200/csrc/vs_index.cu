@@ -77,14 +77,11 @@ __global__ void __launch_bounds__(128) vs_logits_kernel(mi_tensor4 q, mi_tensor4
     for (int u = 0; u < 8; ++u) kv[d + u] = DType<DT>::to_f(hv[u]);
   }
   uint16_t* xo = x + (long long)bh * LQ * S + c;
-  for (int i = 0; i < LQ; ++i) {
+  auto emit = [&](int i, float acc) {
     uint16_t bits;
     if (c > S - LQ + i) {
       bits = DType<DT>::kBF16 ? (uint16_t)0xFF80 : (uint16_t)0xFC00;  // -inf
     } else {
-      float acc = 0.f;
-#pragma unroll
-      for (int d = 0; d < D; ++d) acc = __fmaf_rn(qs[i][d], kv[d], acc);
       const float r1 = DType<DT>::round(acc);
       const float r2 = DType<DT>::round(__fdiv_rn(r1, sqrt_d));
       if (DType<DT>::kBF16) {
@@ -94,6 +91,12 @@ __global__ void __launch_bounds__(128) vs_logits_kernel(mi_tensor4 q, mi_tensor4
       }
     }
     xo[(long long)i * S] = bits;
+  };
+  for (int i = 0; i < LQ; ++i) {
+    float acc = 0.f;
+#pragma unroll
+    for (int d = 0; d < D; ++d) acc = __fmaf_rn(qs[i][d], kv[d], acc);
+    emit(i, acc);
   }
 }
 
@@ -127,12 +130,14 @@ __global__ void __launch_bounds__(1024) vs_rowstats_kernel(const uint16_t* x, in
   if (threadIdx.x == 0) {
     unsigned long long tot = 0;
     for (int w = 0; w < 32; ++w) tot += red_s[w];
-    stats[(long long)bh * LQ + i] = make_float2(m, (float)((double)tot / kFixScale));
+    // {row max, 1 / row sum}: probabilities are exp(x - m) * (1 / l)
+    const float l = (float)((double)tot / kFixScale);
+    stats[(long long)bh * LQ + i] = make_float2(m, __fdiv_rn(1.0f, l));
   }
 }
 
 // ---------------------------------------------------------------------------
-// K3c: p[i][c] = det_exp(x - m_i) / l_i;  vertical[c] = sum_i p[i][c];
+// K3c: p[i][c] = det_exp(x - m_i) * (1 / l_i);  vertical[c] = sum_i p[i][c];
 // slash[t] = sum_i p[i][t + 1 + i - LQ] (columns outside [0,S) add nothing),
 // both summed in row order.  Forced entries (c < 30, t >= S-100) get +inf.
 // Output: order-preserving keys vkeys/skeys [BH][S].
@@ -150,11 +155,11 @@ __global__ void __launch_bounds__(256) vs_sums_kernel(const uint16_t* x, const f
   const uint16_t* xb = x + (long long)bh * LQ * S;
   float vs = 0.f, ds = 0.f;
   for (int i = 0; i < LQ; ++i) {
-    const float pv = __fdiv_rn(det_exp(__fsub_rn(DType<DT>::to_f(xb[(long long)i * S + c]), st[i].x)), st[i].y);
+    const float pv = __fmul_rn(det_exp(__fsub_rn(DType<DT>::to_f(xb[(long long)i * S + c]), st[i].x)), st[i].y);
     vs = __fadd_rn(vs, pv);
     const int col = c + 1 + i - LQ;
     if (col >= 0 && col < S) {
-      const float pd = __fdiv_rn(det_exp(__fsub_rn(DType<DT>::to_f(xb[(long long)i * S + col]), st[i].x)), st[i].y);
+      const float pd = __fmul_rn(det_exp(__fsub_rn(DType<DT>::to_f(xb[(long long)i * S + col]), st[i].x)), st[i].y);
       ds = __fadd_rn(ds, pd);
     }
   }
