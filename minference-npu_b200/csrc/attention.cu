@@ -5,47 +5,21 @@
 
 namespace mib200 {
 
-// Exponential of the P tile (compile-time choice, measured in bench.py runs):
-//   MI_EXP_MODE 0: ex2.approx.f32 on the MUFU unit for every element
-//               1: bf16 only: x rounded to bf16 pairs, one ex2.approx.ftz.bf16x2 per pair
-//                  (half the MUFU operations; P comes out packed)
-//               2: as 0, but one pair in four on the FMA pipe (poly_exp2x2)
-//   MI_PACK_INT 1: bf16 P packed with integer rounding + PRMT (ALU) instead of the
-//                  cvt.rn.bf16x2 conversion, which shares the XU pipe with MUFU
-//   MI_POLY_EVERY  with mode 2: pair c uses the polynomial when c % MI_POLY_EVERY == MI_POLY_EVERY-1
-#ifndef MI_PACK_INT
-#define MI_PACK_INT 0
-#endif
-#ifndef MI_POLY_EVERY
-#define MI_POLY_EVERY 4
-#endif
-#ifndef MI_EXP_MODE
-#define MI_EXP_MODE 0
+#ifdef MI_TRACE
+// Debug builds only (-DMI_TRACE): clock64 timeline of the CTA with blockIdx
+// (0,0,0), [event][entry], read back with mi_debug_trace().
+__device__ unsigned long long g_trace[10][4096];
+#define MI_TR(ev, j) \
+  do { if (trace_cta && (j) < 4096) g_trace[ev][j] = clock64(); } while (0)
+#else
+#define MI_TR(ev, j) do { } while (0)
 #endif
 
-__device__ __forceinline__ uint32_t ex2_bf16x2(uint32_t x) {
-  uint32_t r;
-  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(r) : "r"(x));
-  return r;
-}
-
-// bf16x2 from two non-negative floats: round half up on the dropped 16 bits,
-// keep the high halves (one PRMT).  For P values in [0, 256].
-__device__ __forceinline__ uint32_t pack_bf16_int(float a, float b) {
-  const uint32_t ua = __float_as_uint(a) + 0x8000u;
-  const uint32_t ub = __float_as_uint(b) + 0x8000u;
-  uint32_t r;
-  asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(r) : "r"(ua), "r"(ub));
-  return r;
-}
-
-template <typename DT>
-__device__ __forceinline__ uint32_t pack_p(float a, float b) {
-#if MI_PACK_INT
-  if constexpr (DType<DT>::kBF16) return pack_bf16_int(a, b);
+// MI_POLY_FULL (default 0; measured neutral): in fully visible blocks one exp2 pair in four runs on
+// the FMA pipe (poly_exp2x2) instead of MUFU.
+#ifndef MI_POLY_FULL
+#define MI_POLY_FULL 0
 #endif
-  return DType<DT>::pack2(a, b);
-}
 
 // Softmax of one 64-key block for one query row, in registers.
 // s: raw scores (overwritten).  Returns the block max of raw visible scores.
@@ -85,6 +59,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int h = blockIdx.y;
   const int b = blockIdx.z;
   const int bh = b * p.H + h;
+#ifdef MI_TRACE
+  const bool trace_cta = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 &&
+                         (threadIdx.x == 0 || threadIdx.x == 160);
+#endif
 
   // ---- entry list of this tile -------------------------------------------
   EntrySource src;
@@ -210,6 +188,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int st = j % kKStages;
         if (!mbar_wait(&k_full[st], (j / kKStages) & 1, 104)) return false;
         tc_fence_after();
+        MI_TR(9, j);
         const uint32_t sk = sk0 + st * L::kKVBytes;
         const uint32_t tmem_s = tmem_base + (j & 1) * kBN;
 #pragma unroll
@@ -221,6 +200,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         umma_commit(&s_full[j & 1]);
         umma_commit(&k_empty[st]);
+        MI_TR(5, j);
         return true;
       };
       bool ok = mbar_wait(q_full, 0, 102);
@@ -231,9 +211,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         // thread: tcgen05.mma from one thread execute in issue order.
         if (j + 1 < n_entries && !issue_qk(j + 1)) { ok = false; break; }
         if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, 105)) { ok = false; break; }
+        MI_TR(6, j);
         const int st = j % kVStages;
         if (!mbar_wait(&v_full[st], (j / kVStages) & 1, 106)) { ok = false; break; }
         tc_fence_after();
+        MI_TR(8, j);
         const uint32_t sv = sv0 + st * L::kVBytes;
         const uint32_t tmem_p = tmem_base + (j & 1) * kBN;
 #pragma unroll
@@ -243,6 +225,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         umma_commit(&pv_done[j & 1]);
         umma_commit(&v_empty[st]);
+        MI_TR(7, j);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -264,8 +247,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint64_t mask = (row < 64) ? m0_n : m1_n;
       if (j + 1 < n_entries) src.get(j + 1, kb_n, m0_n, m1_n);  // prefetch next entry
 
+      MI_TR(0, j);
       if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, 107)) { ok = false; break; }
       tc_fence_after();
+      MI_TR(1, j);
 
       const long long key0 = (long long)kb * kBN;
       // Visible keys of this row inside the block:
@@ -308,6 +293,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         tmax = fmaxf(fmax3(mx0, mx1, fmax3(s[60], s[61], s[62])), fmax3(mx2, mx3, s[63]));
       }
+      MI_TR(2, j);
       const float m_new = fmaxf(m_used, tmax * sc);
       const bool need = m_new > m_used + 8.0f;
       if (j == 0) {
@@ -336,33 +322,38 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int c = 0; c < kBN / 2; ++c) pk[c] = 0u;
       } else {
-        const uint64_t sc2 = pk2(sc, sc);
-        const uint64_t nm2 = pk2(-m_used, -m_used);
+        const float nm = -m_used;
+        if (all_full) {
+          // Fully visible block: one pair in four is exponentiated on the FMA pipe
+          // (poly_exp2x2), the rest on MUFU, which is the softmax's throughput limit.
 #pragma unroll
-        for (int c = 0; c < kBN / 2; ++c) {
-          float x0, x1;
-          upk2(ffma2(pk2(s[2 * c], s[2 * c + 1]), sc2, nm2), x0, x1);
-#if MI_EXP_MODE == 1
-          if constexpr (kBF16) {
-            pk[c] = ex2_bf16x2(DType<DT>::pack2(x0, x1));
-            continue;
+          for (int c = 0; c < kBN / 2; ++c) {
+            const float x0 = __fmaf_rn(s[2 * c], sc, nm);
+            const float x1 = __fmaf_rn(s[2 * c + 1], sc, nm);
+            if (MI_POLY_FULL && (c & 3) == 3) {
+              float p0, p1;
+              poly_exp2x2(pk2(fmaxf(x0, -127.f), fmaxf(x1, -127.f)), p0, p1);
+              pk[c] = DType<DT>::pack2(p0, p1);
+            } else {
+              pk[c] = DType<DT>::pack2(fast_exp2(x0), fast_exp2(x1));
+            }
           }
-#elif MI_EXP_MODE == 2
-          if (all_full && (c % MI_POLY_EVERY) == MI_POLY_EVERY - 1) {
-            float p0, p1;
-            poly_exp2x2(pk2(fmaxf(x0, -127.f), fmaxf(x1, -127.f)), p0, p1);
-            pk[c] = pack_p<DT>(p0, p1);
-            continue;
+        } else {
+#pragma unroll
+          for (int c = 0; c < kBN / 2; ++c) {
+            const float x0 = __fmaf_rn(s[2 * c], sc, nm);
+            const float x1 = __fmaf_rn(s[2 * c + 1], sc, nm);
+            pk[c] = DType<DT>::pack2(fast_exp2(x0), fast_exp2(x1));
           }
-#endif
-          pk[c] = pack_p<DT>(fast_exp2(x0), fast_exp2(x1));
         }
       }
+      MI_TR(3, j);
       // P(j) overwrites the first 32 columns of S buffer (j & 1).
       tmem_st32u(tmem_s, pk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[j & 1]);
+      MI_TR(4, j);
     }
 
     // ---- epilogue: O / l -> shared (Q tile area, swizzled) -> TMA store -----
@@ -437,11 +428,16 @@ static int launch_attn_t(const mi_tensor4& q, const mi_tensor4& k, const mi_tens
   if ((rc = make_bnsd_map(&tv, v, prm.B, prm.H, prm.Sk, D, 32, kBN)) != MI_OK) return rc;
   if ((rc = make_bnsd_map(&to, out, prm.B, prm.H, prm.Sq, D, 32, kBM)) != MI_OK) return rc;
   auto kern = attn_fwd_kernel<DT, D>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc) !=
+#ifdef MI_ONE_CTA_PER_SM
+  const int alloc = 160 * 1024;  // experiment: one CTA per SM
+#else
+  const int alloc = L::kAlloc;
+#endif
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, alloc) !=
       cudaSuccess)
     return MI_ERR_LAUNCH;
   dim3 grid(prm.T, prm.H, prm.B);
-  kern<<<grid, kThreads, L::kAlloc, stream>>>(tq, tk, tv, to, prm);
+  kern<<<grid, kThreads, alloc, stream>>>(tq, tk, tv, to, prm);
   return cudaGetLastError() == cudaSuccess ? MI_OK : MI_ERR_LAUNCH;
 }
 
@@ -466,3 +462,11 @@ int launch_attention(const mi_tensor4& q, const mi_tensor4& k, const mi_tensor4&
 }
 
 }  // namespace mib200
+
+#ifdef MI_TRACE
+extern "C" int mi_debug_trace(unsigned long long* host_out) {
+  return cudaMemcpyFromSymbol(host_out, mib200::g_trace, sizeof(mib200::g_trace)) == cudaSuccess
+             ? 0
+             : 4;
+}
+#endif
