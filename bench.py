@@ -358,6 +358,137 @@ def run_reference_arm(args, rank, world) -> None:
     print(json.dumps(line), flush=True)
 
 
+def _rows_ref(q, k, v, rows, vis_rows, scale):
+    """fp32 attention of query `rows` (one head) given their visible sets."""
+    logits = (q[rows].float() @ k.float().T) * scale
+    logits = logits.masked_fill(~vis_rows, float("-inf"))
+    p = torch.nan_to_num(torch.softmax(logits, dim=-1), nan=0.0)
+    return p @ v.float()
+
+
+def _bs_rows_visible(idx_h, rows, S):
+    nb = idx_h.shape[0]
+    blk = torch.zeros(nb, nb, dtype=torch.bool, device=idx_h.device)
+    blk.scatter_(1, idx_h.clamp(0, nb - 1), True)
+    r = torch.as_tensor(rows, device=idx_h.device)
+    j = torch.arange(S, device=idx_h.device)
+    return blk[r // 64][:, j // 64] & (j[None, :] <= r[:, None])
+
+
+def _vs_rows_visible(v_h, s_h, rows, S):
+    dev = v_h.device
+    r = torch.as_tensor(rows, device=dev)
+    end_m = (r // 64 + 1) * 64
+    s = s_h.long()
+    valid = s[None, :] < end_m[:, None]
+    re = (end_m[:, None] - s[None, :]).clamp(min=64).clamp(max=S)
+    rs = (re - 64).clamp(min=0)
+    delta = torch.zeros(len(rows), S + 1, dtype=torch.int32, device=dev)
+    ones = valid.to(torch.int32)
+    delta.scatter_add_(1, torch.where(valid, rs, S), ones)
+    delta.scatter_add_(1, torch.where(valid, re, S), -ones)
+    cov = delta.cumsum(1)[:, :S] > 0
+    cov[:, v_h.long().clamp(0, S - 1)] = True
+    j = torch.arange(S, device=dev)
+    return cov & (j[None, :] <= r[:, None])
+
+
+def run_baseline_configs(args) -> None:
+    """BASELINE configs 0-2 as single-layer ops on 32 heads: device ms (events,
+    index estimation included), effective TFLOP/s vs dense causal, roofline
+    fraction of the attention phase (visible-pair FLOPs at measured bf16 peak)
+    and max |out - fp32| over 256 sampled rows of 4 heads."""
+    from minference import ops
+
+    dev = torch.device("cuda", 0)
+    tf_peak, _, _ = _peaks()
+    H = 32
+    cases = [
+        ("config0 stream_llm S=4096 fp16 n_init=128 n_local=1024", 4096, torch.float16, "stream"),
+        ("config1 block_sparse S=16384 bf16 top-100 + block 0 + diagonal", 16384, torch.bfloat16, "bs"),
+        ("config2 vertical_slash S=32768 bf16 v=1000 s=6096", 32768, torch.bfloat16, "vs"),
+    ]
+    for name, S, dt, kind in cases:
+        q = torch.empty(1, H, S, D, dtype=dt, device=dev)
+        k = torch.empty_like(q)
+        v = torch.empty_like(q)
+        for h in range(H):
+            g = torch.Generator(device=dev).manual_seed(77 + h)
+            q[0, h] = (torch.randn(S, D, generator=g, device=dev) / math.sqrt(D)).to(dt)
+            kk = torch.randn(S, D, generator=g, device=dev) / math.sqrt(D)
+            v[0, h] = (torch.randn(S, D, generator=g, device=dev) / math.sqrt(D)).to(dt)
+            if kind == "bs":
+                u = torch.randn(S, 4, generator=g, device=dev)
+                w = torch.randn(4, D, generator=g, device=dev) / math.sqrt(4 * D)
+                kk = kk + 2.0 * (u @ w)
+            if kind == "vs":
+                pos = torch.randperm(S, generator=g, device=dev)[:32]
+                kk[pos] *= 4.0
+            k[0, h] = kk.to(dt)
+        out = torch.empty_like(q)
+        state = {}
+
+        def step(ev=None):
+            a = b = None
+            if kind == "stream":
+                a = torch.cuda.Event(enable_timing=True); a.record()
+                ops.streaming_forward(q, k, v, ST_INIT, ST_LOCAL, out=out)
+            elif kind == "bs":
+                idx = ops.select_block_sparse_topk_indices(q, k, BS_TOPK, force_sink_diag=True)
+                state["idx"] = idx
+                a = torch.cuda.Event(enable_timing=True); a.record()
+                ops.block_sparse_attention_from_indices(q, k, v, idx, out=out)
+            else:
+                vi, si = ops.vertical_and_slash_estimate(q, k, VS_V, VS_S)
+                state["vi"], state["si"] = vi, si
+                a = torch.cuda.Event(enable_timing=True); a.record()
+                ops.vertical_slash_sparse_attention(q, k, v, vi, si, out=out)
+            b = torch.cuda.Event(enable_timing=True); b.record()
+            if ev is not None:
+                ev.append((a, b))
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        ev = []
+        t0 = torch.cuda.Event(enable_timing=True); t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            step(ev)
+        t1.record()
+        torch.cuda.synchronize()
+        ms = t0.elapsed_time(t1) / args.steps
+        attn_ms = sum(x.elapsed_time(y) for x, y in ev) / args.steps
+        if kind == "stream":
+            vis = stream_visible_pairs(S, ST_INIT, ST_LOCAL) * H
+        elif kind == "bs":
+            vis = sum(bs_visible_pairs(state["idx"][0, h], S) for h in range(H))
+        else:
+            vis = sum(vs_visible_pairs(state["vi"][0, h], state["si"][0, h], S) for h in range(H))
+        dense_flops = dense_causal_flops(S, H)
+        achieved = 4.0 * D * vis / (attn_ms * 1e-3) / 1e12
+        scale = 128 ** -0.5
+        rng = np.random.default_rng(S)
+        rows = sorted(rng.choice(S, 256, replace=False).tolist())
+        err = 0.0
+        for h in (0, 7, 19, 31):
+            if kind == "stream":
+                r = torch.as_tensor(rows, device=dev)[:, None]
+                j = torch.arange(S, device=dev)[None, :]
+                visr = ((j < ST_INIT) | (j > r - ST_LOCAL)) & (j <= r)
+            elif kind == "bs":
+                visr = _bs_rows_visible(state["idx"][0, h], rows, S)
+            else:
+                visr = _vs_rows_visible(state["vi"][0, h], state["si"][0, h], rows, S)
+            ref = _rows_ref(q[0, h], k[0, h], v[0, h], rows, visr, scale)
+            err = max(err, (out[0, h, rows].float() - ref).abs().max().item())
+        print(json.dumps({"config": name, "ms": ms, "attn_ms": attn_ms,
+                          "eff_tflops_vs_dense": dense_flops / (ms * 1e-3) / 1e12,
+                          "visible_fraction": vis / (H * S * (S + 1) / 2),
+                          "roofline_frac": achieved / tf_peak, "max_abs_err_vs_fp32": err}),
+              flush=True)
+
+
 def phi3_mini_config():
     """Phi-3-mini-128k architecture (32 layers, hidden 3072, 32 heads of 96,
     SwiGLU MLP 8192, RMSNorm, vocab 32064, LongRoPE 'su' scaling).  The
@@ -438,6 +569,8 @@ def main():
     ap.add_argument("--ctx", default="4096,8192,16384,32768,65536")
     ap.add_argument("--attn-types", default="minference,dense,hf")
     ap.add_argument("--ttft-runs", type=int, default=2)
+    ap.add_argument("--baseline-configs", action="store_true",
+                    help="BASELINE configs 0-2 as single-layer ops (one JSON line each)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -449,6 +582,10 @@ def main():
         return
     if args.ttft:
         run_ttft(args)
+        return
+    if args.baseline_configs:
+        torch.cuda.set_device(0)
+        run_baseline_configs(args)
         return
     assert args.heads % world == 0, "heads must divide evenly over ranks"
     torch.cuda.set_device(local_rank)
