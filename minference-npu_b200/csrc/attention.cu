@@ -175,60 +175,66 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (!ok) *abort_flag = 1;
     }
   } else if (warp == 5) {
-    // ======================= MMA issuer =======================================
-    if (lane == 0) {
-      constexpr uint32_t idesc_qk = make_idesc_f16(kBF16, kBM, kBN, false, false);
-      constexpr uint32_t idesc_pv = make_idesc_f16(kBF16, kBM, L::kOCols, false, true);
-      const uint32_t sq = smem_u32(smem + L::kQOff);
-      const uint32_t sk0 = smem_u32(smem + L::kKOff);
-      const uint32_t sv0 = smem_u32(smem + L::kVOff);
-      const uint32_t tmem_o = tmem_base + 128;
+    // ======================= MMA issuer (whole warp) ===========================
+    // The warp runs converged and an elected lane issues: a tcgen05.mma issue
+    // takes about as long as the MMA, so every wait and branch between MMAs
+    // is tensor-pipe idle time, and a lone lane in a divergent branch issues
+    // at about half the converged rate.
+    constexpr uint32_t idesc_qk = make_idesc_f16(kBF16, kBM, kBN, false, false);
+    constexpr uint32_t idesc_pv = make_idesc_f16(kBF16, kBM, L::kOCols, false, true);
+    const uint64_t qd0 = make_desc_sw64(smem_u32(smem + L::kQOff), 16, 512);
+    const uint64_t kd0 = make_desc_sw64(smem_u32(smem + L::kKOff), 16, 512);
+    const uint64_t vd0 = make_desc_sw64(smem_u32(smem + L::kVOff), kBN * 64, 512);
+    const uint32_t tmem_o = tmem_base + 128;
 
-      auto issue_qk = [&](int j) -> bool {
-        const int st = j % kKStages;
-        if (!mbar_wait(&k_full[st], (j / kKStages) & 1, 104)) return false;
-        tc_fence_after();
-        MI_TR(9, j);
-        const uint32_t sk = sk0 + st * L::kKVBytes;
+    auto issue_qk = [&](int j) -> bool {
+      const int st = j % kKStages;
+      if (!__all_sync(0xffffffffu, mbar_wait(&k_full[st], (j / kKStages) & 1, 104))) return false;
+      tc_fence_after();
+      MI_TR(9, j);
+      if (elect_one_sync()) {
+        const uint64_t kd = kd0 + (uint64_t)((st * L::kKVBytes) >> 4);
         const uint32_t tmem_s = tmem_base + (j & 1) * kBN;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
           const uint32_t koff = (ks & 1) * 32;
-          const uint64_t ad = make_desc_sw64(sq + (ks >> 1) * (kBM * 64) + koff, 16, 512);
-          const uint64_t bd = make_desc_sw64(sk + (ks >> 1) * (kBN * 64) + koff, 16, 512);
-          umma_f16_ss(tmem_s, ad, bd, idesc_qk, ks > 0 ? 1u : 0u);
+          umma_f16_ss(tmem_s, qd0 + (((ks >> 1) * (kBM * 64) + koff) >> 4),
+                      kd + (((ks >> 1) * (kBN * 64) + koff) >> 4), idesc_qk, ks > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[j & 1]);
         umma_commit(&k_empty[st]);
-        MI_TR(5, j);
-        return true;
-      };
-      bool ok = mbar_wait(q_full, 0, 102);
-      if (ok && n_entries > 0) ok = issue_qk(0);
-      for (int j = 0; ok && j < n_entries; ++j) {
-        if (*abort_flag) { ok = false; break; }
-        // S buffer (j+1)&1 last held P(j-1), consumed by PV(j-1), issued earlier by this
-        // thread: tcgen05.mma from one thread execute in issue order.
-        if (j + 1 < n_entries && !issue_qk(j + 1)) { ok = false; break; }
-        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, 105)) { ok = false; break; }
-        MI_TR(6, j);
-        const int st = j % kVStages;
-        if (!mbar_wait(&v_full[st], (j / kVStages) & 1, 106)) { ok = false; break; }
-        tc_fence_after();
-        MI_TR(8, j);
-        const uint32_t sv = sv0 + st * L::kVBytes;
+      }
+      __syncwarp();
+      MI_TR(5, j);
+      return true;
+    };
+    bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, 102));
+    if (ok && n_entries > 0) ok = issue_qk(0);
+    for (int j = 0; ok && j < n_entries; ++j) {
+      if (*abort_flag) { ok = false; break; }
+      // S buffer (j+1)&1 last held P(j-1), consumed by PV(j-1), issued earlier by this
+      // warp: tcgen05.mma from one thread execute in issue order.
+      if (j + 1 < n_entries && !issue_qk(j + 1)) { ok = false; break; }
+      const int st = j % kVStages;
+      if (!__all_sync(0xffffffffu, mbar_wait(&p_full[j & 1], (j >> 1) & 1, 105))) { ok = false; break; }
+      MI_TR(6, j);
+      if (!__all_sync(0xffffffffu, mbar_wait(&v_full[st], (j / kVStages) & 1, 106))) { ok = false; break; }
+      tc_fence_after();
+      MI_TR(8, j);
+      if (elect_one_sync()) {
+        const uint64_t vd = vd0 + (uint64_t)((st * L::kVBytes) >> 4);
         const uint32_t tmem_p = tmem_base + (j & 1) * kBN;
 #pragma unroll
-        for (int ks = 0; ks < kBN / 16; ++ks) {
-          const uint64_t bd = make_desc_sw64(sv + ks * 1024, kBN * 64, 512);
-          umma_f16_ts(tmem_o, tmem_p + ks * 8, bd, idesc_pv, (j > 0 || ks > 0) ? 1u : 0u);
-        }
+        for (int ks = 0; ks < kBN / 16; ++ks)
+          umma_f16_ts(tmem_o, tmem_p + ks * 8, vd + (uint64_t)((ks * 1024) >> 4), idesc_pv,
+                      (j > 0 || ks > 0) ? 1u : 0u);
         umma_commit(&pv_done[j & 1]);
         umma_commit(&v_empty[st]);
-        MI_TR(7, j);
       }
-      if (!ok) *abort_flag = 1;
+      __syncwarp();
+      MI_TR(7, j);
     }
+    if (!ok && lane == 0) *abort_flag = 1;
   } else {
     // ======================= softmax warps 0-3 ================================
     const int row = threadIdx.x;  // 0..127

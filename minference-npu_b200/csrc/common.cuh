@@ -177,6 +177,20 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
       : "memory");
 }
 
+// True in exactly one lane of the (converged) warp.  tcgen05.mma is issued at
+// the tensor pipe's full rate when the issuing warp runs converged and one
+// elected lane issues (measured on B200: ~64 cycles per M=128,N=128,K=16 MMA);
+// from a lone lane inside a divergent branch each MMA costs ~115-125 cycles.
+__device__ __forceinline__ bool elect_one_sync() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .b32 %%rx;\n\t.reg .pred %%px;\n\t"
+      "elect.sync %%rx|%%px, %1;\n\t@%%px mov.s32 %0, 1;\n\t}"
+      : "+r"(pred)
+      : "r"(0xffffffffu));
+  return pred != 0;
+}
+
 // Arrive on an mbarrier once all previously issued tcgen05.mma of this thread complete.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile(
