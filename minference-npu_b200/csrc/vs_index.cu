@@ -50,53 +50,107 @@ constexpr double kFixScale = 17592186044416.0;  // 2^44: row sums in 64-bit fixe
 // K3a: logits x[i][c] for the last LQ queries, rounded like the reference:
 // round_dt(round_dt(dot) / sqrt_d); masked (c > S-LQ+i) entries are -inf.
 // Stored as the input dtype's bits: x: [BH][LQ][S] uint16.
-// Grid (ceil(S/128), H, B), 128 threads: thread = one key column.
+// Grid (ceil(S/128), H, B), 128 threads; one CTA = 64 query rows x 128 keys.
+// Warp w owns rows [16w, 16w+16), lane l owns keys [4l, 4l+4): 64 independent
+// fmaf chains per thread.  Each (row, key) dot product is still one chain
+// over d = 0..D-1 in order, so the result is the oracle's bit for bit.  Q
+// and the K tile are staged in shared memory as fp32, transposed ([d][row],
+// [d][key]): one step over d reads one float4 of keys and four float4 of
+// rows (the rows are the same for the whole warp: a broadcast).
 // ---------------------------------------------------------------------------
+constexpr int kLgRows = 64, kLgKeys = 128;
+
+template <int D>
+constexpr int vs_logits_smem_bytes() {
+  return (kLgRows + kLgKeys) * D * 4;
+}
+
 template <typename DT, int D>
 __global__ void __launch_bounds__(128) vs_logits_kernel(mi_tensor4 q, mi_tensor4 k, int H, int S,
                                                         int LQ, float sqrt_d, uint16_t* x) {
-  __shared__ float qs[64][D];
+  extern __shared__ float4 lg_smem4[];
+  float* qs = reinterpret_cast<float*>(lg_smem4);  // [D][64]
+  float* ks = qs + D * kLgRows;                     // [D][128]
   const int h = blockIdx.y, b = blockIdx.z, bh = b * H + h;
+  const int key0 = blockIdx.x * kLgKeys;
   const uint16_t* qb = reinterpret_cast<const uint16_t*>(q.ptr) + (long long)b * q.stride_b +
                        (long long)h * q.stride_h;
-  for (int e = threadIdx.x; e < LQ * D; e += blockDim.x) {
-    const int i = e / D, d = e % D;
-    qs[i][d] = DType<DT>::to_f(qb[(long long)(S - LQ + i) * q.stride_s + d]);
+  for (int e = threadIdx.x; e < kLgRows * D; e += blockDim.x) {
+    const int i = e % kLgRows, d = e / kLgRows;
+    qs[d * kLgRows + i] =
+        i < LQ ? DType<DT>::to_f(qb[(long long)(S - LQ + i) * q.stride_s + d]) : 0.f;
+  }
+  {
+    const int c = key0 + threadIdx.x;
+    const uint16_t* kr = reinterpret_cast<const uint16_t*>(k.ptr) + (long long)b * k.stride_b +
+                         (long long)h * k.stride_h + (long long)c * k.stride_s;
+#pragma unroll
+    for (int d = 0; d < D; d += 8) {
+      uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+      if (c < S) raw = *reinterpret_cast<const uint4*>(kr + d);
+      const uint16_t* hv = reinterpret_cast<const uint16_t*>(&raw);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) ks[(d + u) * kLgKeys + threadIdx.x] = DType<DT>::to_f(hv[u]);
+    }
   }
   __syncthreads();
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= S) return;
-  const uint16_t* kr = reinterpret_cast<const uint16_t*>(k.ptr) + (long long)b * k.stride_b +
-                       (long long)h * k.stride_h + (long long)c * k.stride_s;
-  float kv[D];
+
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const float4* ks4 = reinterpret_cast<const float4*>(ks);
+  const float4* qs4 = reinterpret_cast<const float4*>(qs);
+  float acc[16][4];
 #pragma unroll
-  for (int d = 0; d < D; d += 8) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(kr + d);
-    const uint16_t* hv = reinterpret_cast<const uint16_t*>(&raw);
+  for (int r = 0; r < 16; ++r)
 #pragma unroll
-    for (int u = 0; u < 8; ++u) kv[d + u] = DType<DT>::to_f(hv[u]);
-  }
-  uint16_t* xo = x + (long long)bh * LQ * S + c;
-  auto emit = [&](int i, float acc) {
-    uint16_t bits;
-    if (c > S - LQ + i) {
-      bits = DType<DT>::kBF16 ? (uint16_t)0xFF80 : (uint16_t)0xFC00;  // -inf
-    } else {
-      const float r1 = DType<DT>::round(acc);
-      const float r2 = DType<DT>::round(__fdiv_rn(r1, sqrt_d));
-      if (DType<DT>::kBF16) {
-        bits = (uint16_t)(__float_as_uint(r2) >> 16);
-      } else {
-        bits = __half_as_ushort(__float2half_rn(r2));
+    for (int u = 0; u < 4; ++u) acc[r][u] = 0.f;
+#pragma unroll 2
+  for (int d = 0; d < D; ++d) {
+    const float4 kv = ks4[d * (kLgKeys / 4) + l];
+#pragma unroll
+    for (int r4 = 0; r4 < 4; ++r4) {
+      const float4 qv = qs4[d * (kLgRows / 4) + w * 4 + r4];
+      const float qr[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float* a = acc[r4 * 4 + u];
+        a[0] = __fmaf_rn(qr[u], kv.x, a[0]);
+        a[1] = __fmaf_rn(qr[u], kv.y, a[1]);
+        a[2] = __fmaf_rn(qr[u], kv.z, a[2]);
+        a[3] = __fmaf_rn(qr[u], kv.w, a[3]);
       }
     }
-    xo[(long long)i * S] = bits;
-  };
-  for (int i = 0; i < LQ; ++i) {
-    float acc = 0.f;
+  }
+
+  const uint16_t neg_inf = DType<DT>::kBF16 ? (uint16_t)0xFF80 : (uint16_t)0xFC00;
+  const int c0 = key0 + 4 * l;
+  const bool vec = (S % 4 == 0) && (c0 + 3 < S);
 #pragma unroll
-    for (int d = 0; d < D; ++d) acc = __fmaf_rn(qs[i][d], kv[d], acc);
-    emit(i, acc);
+  for (int r = 0; r < 16; ++r) {
+    const int i = w * 16 + r;
+    if (i >= LQ) break;
+    uint16_t bits[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int c = c0 + u;
+      if (c > S - LQ + i) {
+        bits[u] = neg_inf;
+      } else {
+        const float r1 = DType<DT>::round(acc[r][u]);
+        const float r2 = DType<DT>::round(__fdiv_rn(r1, sqrt_d));
+        bits[u] = DType<DT>::kBF16 ? (uint16_t)(__float_as_uint(r2) >> 16)
+                                   : __half_as_ushort(__float2half_rn(r2));
+      }
+    }
+    uint16_t* xo = x + ((long long)bh * LQ + i) * S;
+    if (vec) {
+      *reinterpret_cast<uint2*>(xo + c0) =
+          make_uint2((uint32_t)bits[0] | ((uint32_t)bits[1] << 16),
+                     (uint32_t)bits[2] | ((uint32_t)bits[3] << 16));
+    } else {
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (c0 + u < S) xo[c0 + u] = bits[u];
+    }
   }
 }
 
@@ -350,8 +404,10 @@ extern "C" size_t mi_vs_estimate_workspace_size(int64_t B, int64_t H, int64_t S)
 template <typename DT, int D>
 static void launch_vs_logits(const mi_tensor4& q, const mi_tensor4& k, int64_t B, int64_t H,
                              int64_t S, int LQ, float sqrt_d, uint16_t* x, cudaStream_t st) {
-  dim3 g((unsigned)((S + 127) / 128), (unsigned)H, (unsigned)B);
-  vs_logits_kernel<DT, D><<<g, 128, 0, st>>>(q, k, (int)H, (int)S, LQ, sqrt_d, x);
+  dim3 g((unsigned)((S + kLgKeys - 1) / kLgKeys), (unsigned)H, (unsigned)B);
+  constexpr int smem = vs_logits_smem_bytes<D>();
+  cudaFuncSetAttribute(vs_logits_kernel<DT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  vs_logits_kernel<DT, D><<<g, 128, smem, st>>>(q, k, (int)H, (int)S, LQ, sqrt_d, x);
 }
 
 extern "C" int mi_vs_estimate(mi_tensor4 q, mi_tensor4 k, int64_t B, int64_t H, int64_t S,

@@ -219,6 +219,7 @@ VS_EST_CASES = [
     (2048, 96, torch.float16, 200, 300, 8),
     (4096, 128, torch.bfloat16, 1000, 1500, 32),
     (50, 64, torch.bfloat16, 30, 50, 2),
+    (1001, 64, torch.float16, 100, 150, 4),
 ]
 
 
