@@ -28,14 +28,26 @@ struct RowState {
   float l;       // running sum of P
 };
 
-template <typename DT, int D>
+// SPLIT (block_sparse plans): each entry carries one key block per 64-row
+// half of the tile.  S and O of the two halves are computed by two M=64 MMAs
+// whose accumulators interleave in TMEM: the M=64 layout puts row m of the
+// MMA at lane (m % 16) + 32 * (m / 16), and the second MMA, addressed at lane
+// 16, fills the other 16 lanes of every 32-lane quadrant.  Query row r of
+// the tile therefore sits at a lane where each quadrant holds 16 rows of
+// each half; softmax thread L owns row split_row(L).
+__device__ __forceinline__ int split_row(int L) {
+  return ((L & 31) < 16) ? (L >> 5) * 16 + (L & 15) : 64 + (L >> 5) * 16 + (L & 15);
+}
+
+template <typename DT, int D, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v,
                     const __grid_constant__ CUtensorMap tm_o, const AttnParams p) {
-  using L = AttnSmem<D>;
+  using L = AttnSmem<D, SPLIT>;
   constexpr int NC = L::NC;
+  constexpr int KS = L::KS, VS = L::VS;
   constexpr bool kBF16 = DType<DT>::kBF16;
 
   extern __shared__ uint8_t smem_raw[];
@@ -44,10 +56,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* q_full = bars;
   uint64_t* k_full = q_full + 1;
-  uint64_t* k_empty = k_full + kKStages;
-  uint64_t* v_full = k_empty + kKStages;
-  uint64_t* v_empty = v_full + kVStages;
-  uint64_t* s_full = v_empty + kVStages;
+  uint64_t* k_empty = k_full + KS;
+  uint64_t* v_full = k_empty + KS;
+  uint64_t* v_empty = v_full + VS;
+  uint64_t* s_full = v_empty + VS;
   uint64_t* p_full = s_full + 2;
   uint64_t* pv_done = p_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlotOff);
@@ -95,11 +107,11 @@ __global__ void __launch_bounds__(kThreads, 2)
   // ---- one-time setup -------------------------------------------------------
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < kKStages; ++s) {
+    for (int s = 0; s < KS; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
     }
-    for (int s = 0; s < kVStages; ++s) {
+    for (int s = 0; s < VS; ++s) {
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
@@ -113,8 +125,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   // Constant chunk NC of every V stage: column 0 = 1, other columns 0 (64-byte
   // swizzled like the TMA-loaded chunks).  TMA never writes it.
-  for (int i = threadIdx.x; i < kVStages * kBN * 4; i += kThreads) {
-    const int st = i / (kBN * 4), r = (i >> 2) % kBN, lu = i & 3;
+  for (int i = threadIdx.x; i < VS * L::NB * kBN * 4; i += kThreads) {
+    const int st = i / (kBN * 4), r = (i >> 2) % kBN, lu = i & 3;  // st: block slot of the V ring
     const uint16_t one = DType<DT>::kBF16 ? (uint16_t)0x3F80 : (uint16_t)0x3C00;
     const uint4 val = make_uint4(lu == 0 ? (uint32_t)one : 0u, 0u, 0u, 0u);
     *reinterpret_cast<uint4*>(smem + L::kVOff + st * L::kVBytes + NC * (kBN * 64) + r * 64 +
@@ -141,28 +153,34 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_arrive_expect_tx(q_full, L::kQBytes);
       for (int c = 0; c < NC; ++c)
         tma_load_4d(smem + L::kQOff + c * (kBM * 64), &tm_q, q_full, c * 32, t * kBM, h, b);
+      // A stage holds one key block per entry, or two in a split tile
+      // (the block of query rows [0,64), then the block of rows [64,128)).
       auto load_k = [&](int j) -> bool {
-        const int st = j % kKStages, use = j / kKStages;
+        const int st = j % KS, use = j / KS;
         if (use > 0 && !mbar_wait(&k_empty[st], (use - 1) & 1, 101)) return false;
-        int kb;
+        int kb[2];
         uint64_t m0, m1;
-        src.get(j, kb, m0, m1);
-        uint8_t* dst = smem + L::kKOff + st * L::kKVBytes;
-        mbar_arrive_expect_tx(&k_full[st], L::kKVBytes);
-        for (int c = 0; c < NC; ++c)
-          tma_load_4d(dst + c * (kBN * 64), &tm_k, &k_full[st], c * 32, kb * kBN, h, b);
+        src.get(j, kb[0], kb[1], m0, m1);
+        uint8_t* dst = smem + L::kKOff + st * L::kKStage;
+        mbar_arrive_expect_tx(&k_full[st], L::kKStage);
+        for (int hb = 0; hb < L::NB; ++hb)
+          for (int c = 0; c < NC; ++c)
+            tma_load_4d(dst + hb * L::kKVBytes + c * (kBN * 64), &tm_k, &k_full[st], c * 32,
+                        kb[hb] * kBN, h, b);
         return true;
       };
       auto load_v = [&](int j) -> bool {
-        const int st = j % kVStages, use = j / kVStages;
+        const int st = j % VS, use = j / VS;
         if (use > 0 && !mbar_wait(&v_empty[st], (use - 1) & 1, 103)) return false;
-        int kb;
+        int kb[2];
         uint64_t m0, m1;
-        src.get(j, kb, m0, m1);
-        uint8_t* dst = smem + L::kVOff + st * L::kVBytes;
-        mbar_arrive_expect_tx(&v_full[st], L::kKVBytes);
-        for (int c = 0; c < NC; ++c)
-          tma_load_4d(dst + c * (kBN * 64), &tm_v, &v_full[st], c * 32, kb * kBN, h, b);
+        src.get(j, kb[0], kb[1], m0, m1);
+        uint8_t* dst = smem + L::kVOff + st * L::kVStage;
+        mbar_arrive_expect_tx(&v_full[st], L::NB * L::kKVBytes);
+        for (int hb = 0; hb < L::NB; ++hb)
+          for (int c = 0; c < NC; ++c)
+            tma_load_4d(dst + hb * L::kVBytes + c * (kBN * 64), &tm_v, &v_full[st], c * 32,
+                        kb[hb] * kBN, h, b);
         return true;
       };
       bool ok = true;
@@ -180,26 +198,34 @@ __global__ void __launch_bounds__(kThreads, 2)
     // takes about as long as the MMA, so every wait and branch between MMAs
     // is tensor-pipe idle time, and a lone lane in a divergent branch issues
     // at about half the converged rate.
-    constexpr uint32_t idesc_qk = make_idesc_f16(kBF16, kBM, kBN, false, false);
-    constexpr uint32_t idesc_pv = make_idesc_f16(kBF16, kBM, L::kOCols, false, true);
+    // Split tiles: two M=64 MMAs per step; the second (query rows [64,128),
+    // its own key block) accumulates at TMEM lane 16.
+    constexpr int kM = SPLIT ? 64 : kBM;
+    constexpr uint32_t idesc_qk = make_idesc_f16(kBF16, kM, kBN, false, false);
+    constexpr uint32_t idesc_pv = make_idesc_f16(kBF16, kM, L::kOCols, false, true);
+    constexpr uint32_t kLane16 = 16u << 16;
     const uint64_t qd0 = make_desc_sw64(smem_u32(smem + L::kQOff), 16, 512);
     const uint64_t kd0 = make_desc_sw64(smem_u32(smem + L::kKOff), 16, 512);
     const uint64_t vd0 = make_desc_sw64(smem_u32(smem + L::kVOff), kBN * 64, 512);
     const uint32_t tmem_o = tmem_base + 128;
 
     auto issue_qk = [&](int j) -> bool {
-      const int st = j % kKStages;
-      if (!__all_sync(0xffffffffu, mbar_wait(&k_full[st], (j / kKStages) & 1, 104))) return false;
+      const int st = j % KS;
+      if (!__all_sync(0xffffffffu, mbar_wait(&k_full[st], (j / KS) & 1, 104))) return false;
       tc_fence_after();
       MI_TR(9, j);
       if (elect_one_sync()) {
-        const uint64_t kd = kd0 + (uint64_t)((st * L::kKVBytes) >> 4);
+        const uint64_t kd = kd0 + (uint64_t)((st * L::kKStage) >> 4);
         const uint32_t tmem_s = tmem_base + (j & 1) * kBN;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
           const uint32_t koff = (ks & 1) * 32;
-          umma_f16_ss(tmem_s, qd0 + (((ks >> 1) * (kBM * 64) + koff) >> 4),
-                      kd + (((ks >> 1) * (kBN * 64) + koff) >> 4), idesc_qk, ks > 0 ? 1u : 0u);
+          const uint64_t qd = qd0 + (((ks >> 1) * (kBM * 64) + koff) >> 4);
+          const uint64_t kdk = kd + (((ks >> 1) * (kBN * 64) + koff) >> 4);
+          umma_f16_ss(tmem_s, qd, kdk, idesc_qk, ks > 0 ? 1u : 0u);
+          if constexpr (SPLIT)  // Q rows [64,128) start 64 rows (4096 B) into each chunk
+            umma_f16_ss(tmem_s + kLane16, qd + ((64 * 64) >> 4), kdk + (L::kKVBytes >> 4),
+                        idesc_qk, ks > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[j & 1]);
         umma_commit(&k_empty[st]);
@@ -215,19 +241,23 @@ __global__ void __launch_bounds__(kThreads, 2)
       // S buffer (j+1)&1 last held P(j-1), consumed by PV(j-1), issued earlier by this
       // warp: tcgen05.mma from one thread execute in issue order.
       if (j + 1 < n_entries && !issue_qk(j + 1)) { ok = false; break; }
-      const int st = j % kVStages;
+      const int st = j % VS;
       if (!__all_sync(0xffffffffu, mbar_wait(&p_full[j & 1], (j >> 1) & 1, 105))) { ok = false; break; }
       MI_TR(6, j);
-      if (!__all_sync(0xffffffffu, mbar_wait(&v_full[st], (j / kVStages) & 1, 106))) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, mbar_wait(&v_full[st], (j / VS) & 1, 106))) { ok = false; break; }
       tc_fence_after();
       MI_TR(8, j);
       if (elect_one_sync()) {
-        const uint64_t vd = vd0 + (uint64_t)((st * L::kVBytes) >> 4);
+        const uint64_t vd = vd0 + (uint64_t)((st * L::kVStage) >> 4);
         const uint32_t tmem_p = tmem_base + (j & 1) * kBN;
 #pragma unroll
-        for (int ks = 0; ks < kBN / 16; ++ks)
-          umma_f16_ts(tmem_o, tmem_p + ks * 8, vd + (uint64_t)((ks * 1024) >> 4), idesc_pv,
-                      (j > 0 || ks > 0) ? 1u : 0u);
+        for (int ks = 0; ks < kBN / 16; ++ks) {
+          const uint64_t vdk = vd + (uint64_t)((ks * 1024) >> 4);
+          umma_f16_ts(tmem_o, tmem_p + ks * 8, vdk, idesc_pv, (j > 0 || ks > 0) ? 1u : 0u);
+          if constexpr (SPLIT)  // P and O of rows [64,128) at lane 16; their V block second
+            umma_f16_ts(tmem_o + kLane16, tmem_p + kLane16 + ks * 8, vdk + (L::kVBytes >> 4),
+                        idesc_pv, (j > 0 || ks > 0) ? 1u : 0u);
+        }
         umma_commit(&pv_done[j & 1]);
         umma_commit(&v_empty[st]);
       }
@@ -237,21 +267,28 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (!ok && lane == 0) *abort_flag = 1;
   } else {
     // ======================= softmax warps 0-3 ================================
-    const int row = threadIdx.x;  // 0..127
+    // Thread = TMEM lane; the query row it owns (identity unless SPLIT).
+    const int row = SPLIT ? split_row(threadIdx.x) : threadIdx.x;
     const uint32_t lane_base = tmem_base + ((uint32_t)(warp * 32) << 16);
     const long long a = (long long)p.q_off + (long long)t * kBM + row;  // absolute position
+    // Lowest and highest absolute positions among the warp's 32 rows.
+    const long long tile_a0 = (long long)p.q_off + (long long)t * kBM;
+    const long long a_w0 = SPLIT ? tile_a0 + warp * 16 : a - lane;
+    const long long a_w1 = SPLIT ? tile_a0 + 64 + warp * 16 + 15 : a - lane + 31;
     const float NEG_INF = -INFINITY;
     const float sc = p.scale_log2;
     float m_used = NEG_INF;
     bool ok = true;
 
-    int kb_n = 0;
+    int kb_n = 0, kb1_n = 0;
     uint64_t m0_n = 0, m1_n = 0;
-    if (n_entries > 0) src.get(0, kb_n, m0_n, m1_n);
+    if (n_entries > 0) src.get(0, kb_n, kb1_n, m0_n, m1_n);
     for (int j = 0; j < n_entries; ++j) {
-      const int kb = kb_n;
+      const int kb = (row < 64) ? kb_n : kb1_n;  // this row's key block
+      const int kb_lo = min(kb_n, kb1_n), kb_hi = max(kb_n, kb1_n);
       const uint64_t mask = (row < 64) ? m0_n : m1_n;
-      if (j + 1 < n_entries) src.get(j + 1, kb_n, m0_n, m1_n);  // prefetch next entry
+      const bool masks_full = (m0_n & m1_n) == ~0ull;
+      if (j + 1 < n_entries) src.get(j + 1, kb_n, kb1_n, m0_n, m1_n);  // prefetch next entry
 
       MI_TR(0, j);
       if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, 107)) { ok = false; break; }
@@ -261,11 +298,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       const long long key0 = (long long)kb * kBN;
       // Visible keys of this row inside the block:
       //   mask AND key <= a AND key < Sk AND (key < n_init OR key > a - n_local).
-      // Warp-uniform shortcut for blocks wholly visible to the warp's 32 rows.
-      const long long a_w0 = a - lane, a_w1 = a - lane + 31;
-      const bool fast_full = (mask == ~0ull) && key0 + kBN - 1 <= a_w0 &&
-                             key0 + kBN - 1 < p.Sk &&
-                             (key0 > a_w1 - p.n_local || key0 + kBN - 1 < p.n_init);
+      // Warp-uniform shortcut for blocks wholly visible to the warp's 32 rows
+      // (evaluated on both halves' masks and key blocks, so it is uniform in
+      // split tiles too, where a warp holds rows of both halves).
+      const long long klo = (long long)kb_lo * kBN, khi = (long long)kb_hi * kBN;
+      const bool fast_full = masks_full && khi + kBN - 1 <= a_w0 && khi + kBN - 1 < p.Sk &&
+                             (klo > a_w1 - p.n_local || khi + kBN - 1 < p.n_init);
       uint64_t vis = ~0ull;
       bool all_full = true, all_empty = false;
       if (!fast_full) {
@@ -423,22 +461,18 @@ __global__ void __launch_bounds__(kThreads, 2)
 // ---------------------------------------------------------------------------
 // Host launcher
 // ---------------------------------------------------------------------------
-template <typename DT, int D>
+template <typename DT, int D, bool SPLIT>
 static int launch_attn_t(const mi_tensor4& q, const mi_tensor4& k, const mi_tensor4& v,
                          const mi_tensor4& out, AttnParams prm, cudaStream_t stream) {
-  using L = AttnSmem<D>;
+  using L = AttnSmem<D, SPLIT>;
   CUtensorMap tq, tk, tv, to;
   int rc;
   if ((rc = make_bnsd_map(&tq, q, prm.B, prm.H, prm.Sq, D, 32, kBM)) != MI_OK) return rc;
   if ((rc = make_bnsd_map(&tk, k, prm.B, prm.H, prm.Sk, D, 32, kBN)) != MI_OK) return rc;
   if ((rc = make_bnsd_map(&tv, v, prm.B, prm.H, prm.Sk, D, 32, kBN)) != MI_OK) return rc;
   if ((rc = make_bnsd_map(&to, out, prm.B, prm.H, prm.Sq, D, 32, kBM)) != MI_OK) return rc;
-  auto kern = attn_fwd_kernel<DT, D>;
-#ifdef MI_ONE_CTA_PER_SM
-  const int alloc = 160 * 1024;  // experiment: one CTA per SM
-#else
+  auto kern = attn_fwd_kernel<DT, D, SPLIT>;
   const int alloc = L::kAlloc;
-#endif
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, alloc) !=
       cudaSuccess)
     return MI_ERR_LAUNCH;
@@ -456,10 +490,16 @@ int launch_attention(const mi_tensor4& q, const mi_tensor4& k, const mi_tensor4&
   prm.os_s = out.stride_s;
   if (prm.T == 0 || prm.H == 0 || prm.B == 0) return MI_OK;
   const bool bf = dtype == MI_BF16;
-#define MI_ATTN_CASE(DD)                                                            \
-  if (D == DD)                                                                     \
-    return bf ? launch_attn_t<__nv_bfloat16, DD>(q, k, v, out, prm, stream)        \
-              : launch_attn_t<__half, DD>(q, k, v, out, prm, stream);
+  const bool split = prm.split != 0;
+  if (split && prm.mode != 1) return MI_ERR_SHAPE;
+#define MI_ATTN_CASE(DD)                                                                  \
+  if (D == DD) {                                                                         \
+    if (split)                                                                           \
+      return bf ? launch_attn_t<__nv_bfloat16, DD, true>(q, k, v, out, prm, stream)      \
+                : launch_attn_t<__half, DD, true>(q, k, v, out, prm, stream);            \
+    return bf ? launch_attn_t<__nv_bfloat16, DD, false>(q, k, v, out, prm, stream)       \
+              : launch_attn_t<__half, DD, false>(q, k, v, out, prm, stream);             \
+  }
   MI_ATTN_CASE(64)
   MI_ATTN_CASE(96)
   MI_ATTN_CASE(128)

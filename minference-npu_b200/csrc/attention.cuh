@@ -11,30 +11,34 @@
 //     partial softmaxes merge inside one online softmax (no LSE merge pass).
 //   * block_sparse and vertical_and_slash (mode 1): entries come from a plan
 //     written by the index kernels (block_sparse.cu / vs_index.cu).
+//   * split tiles (block_sparse): each 64-row half of the tile walks its own
+//     list; an entry names one key block per half, computed by two M=64 MMAs
+//     that share the TMEM lanes (see attn_fwd_kernel).
 // Causality (key <= absolute query position) is always applied per element.
 //
 // Warp roles (192 threads):
-//   warps 0-3  softmax: thread r owns query row r of the tile; reads S from
-//              TMEM, applies masks, online softmax in registers (exp2 on the
-//              MUFU unit for 3/4 of the elements, a degree-3 polynomial on the
-//              FMA pipe for the rest), writes P (bf16/fp16) back into the same
-//              TMEM columns, rescales O in TMEM when the running max grows by
-//              more than 2^8, final normalisation and TMA store of the tile.
-//   warp 4     TMA producer: Q once, then K blocks into a 4-deep ring and V
-//              blocks into a 3-deep ring (K runs ahead because S = QK^T is
-//              issued one block ahead of O += PV).
-//   warp 5     TMEM allocator + single-thread tcgen05.mma issuer:
-//              S = Q K^T (M=128, N=64, K=D, both operands in shared memory)
-//              into a double-buffered TMEM tile; O += P V (M=128, N=D, K=64)
-//              with P read from TMEM and V from shared memory.
+//   warps 0-3  softmax: each thread owns one query row of the tile; reads S
+//              from TMEM, applies masks, online softmax in registers (exp2 on
+//              the MUFU unit), writes P (bf16/fp16) back into the same TMEM
+//              columns, rescales O in TMEM when the running max grows by more
+//              than 2^8, final normalisation and TMA store of the tile.
+//   warp 4     TMA producer: Q once, then K blocks and V blocks into rings
+//              (K runs ahead because S = QK^T is issued one entry ahead of
+//              O += PV).
+//   warp 5     TMEM allocator and tcgen05.mma issuer (converged warp, one
+//              elected lane issues): S = Q K^T (M=128, N=64, K=D, both
+//              operands in shared memory) into a double-buffered TMEM tile;
+//              O += P V (M=128, N=D+16, K=64) with P read from TMEM and V from
+//              shared memory; V carries a ones column, so O column D is the
+//              row sum of P.
 #pragma once
 #include "common.cuh"
 
 namespace mib200 {
 
 struct PlanEntry {
-  int32_t kb;   // key block index (keys [64*kb, 64*kb+64))
-  int32_t pad;
+  int32_t kb;   // key block index (keys [64*kb, 64*kb+64)) of query rows [0,64)
+  int32_t kb1;  // key block of query rows [64,128): equal to kb except in split tiles
   uint64_t m0;  // visible-column mask for query rows [0,64) of the tile
   uint64_t m1;  // visible-column mask for query rows [64,128) of the tile
 };
@@ -62,6 +66,7 @@ struct AttnParams {
   const int* plan_count;       // mode 1: [B*H][T]
   long long plan_cap;          // mode 1
   long long plan_head_stride;  // mode 1: entries per (b,h)
+  int split;                   // 1: split tiles (each half of the tile has its own key block)
 };
 
 constexpr int kBM = 128;       // query rows per CTA
@@ -70,30 +75,45 @@ constexpr int kKStages = 3;    // K ring depth (K runs ahead of V)
 constexpr int kVStages = 3;    // V ring depth
 constexpr int kThreads = 192;
 
-template <int D>
+// Ring depths.  A split tile stages two key blocks per entry (one per query
+// half), so its rings are shallower where two CTAs share an SM (D <= 96; at
+// D = 128 O needs more than half of TMEM and one CTA runs per SM).
+template <int D, bool SPLIT>
+struct RingDepth {
+  static constexpr int K = SPLIT ? 2 : kKStages;
+  static constexpr int V = SPLIT ? (D == 96 ? 1 : 2) : kVStages;
+};
+
+template <int D, bool SPLIT = false>
 struct AttnSmem {
+  static constexpr int NB = SPLIT ? 2 : 1;          // key blocks per entry
+  static constexpr int KS = RingDepth<D, SPLIT>::K;
+  static constexpr int VS = RingDepth<D, SPLIT>::V;
   static constexpr int NC = D / 32;                 // 64-byte chunks per row
   static constexpr int kQBytes = NC * kBM * 64;     // Q tile (reused for the output tile)
   static constexpr int kKVBytes = NC * kBN * 64;    // one K block (and the loaded part of V)
   // A V stage holds NC loaded chunks plus one constant chunk whose first column
   // is all ones: O += P V then also produces the row sums of P in O column D.
   static constexpr int kVBytes = (NC + 1) * kBN * 64;
+  static constexpr int kKStage = NB * kKVBytes;     // one K ring stage
+  static constexpr int kVStage = NB * kVBytes;      // one V ring stage
   static constexpr int kOCols = D + 16;             // O columns incl. the row-sum column
   // TMEM: S0 [0,64), S1 [64,128), O [128, 128+kOCols); P(j) aliases S(j&1)
   static constexpr uint32_t kTmemCols = (128 + kOCols <= 256) ? 256u : 512u;
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kQOff + kQBytes;
-  static constexpr int kVOff = kKOff + kKStages * kKVBytes;
-  static constexpr int kBarOff = kVOff + kVStages * kVBytes;
+  static constexpr int kVOff = kKOff + KS * kKStage;
+  static constexpr int kBarOff = kVOff + VS * kVStage;
   // barriers: q_full, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
   //           s_full[2], p_full[2], pv_done[2]
-  static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 6;
+  static constexpr int kNumBars = 1 + 2 * KS + 2 * VS + 6;
   static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
   static constexpr int kAbortOff = kTmemSlotOff + 4;
   static constexpr int kBytes = kAbortOff + 4;
   // +1 KiB to align the base; never less than ~80 KiB so at most two CTAs
   // share an SM (two CTAs use all 512 TMEM columns).
   static constexpr int kAlloc = (kBytes + 1024) > 80 * 1024 ? (kBytes + 1024) : 80 * 1024;
+  static_assert(kTmemCols == 512 || kAlloc <= 113 * 1024, "two CTAs per SM");
 };
 
 // Entry j of the current tile (identical result in every warp that asks).
@@ -105,14 +125,17 @@ struct EntrySource {
   // mode 1
   const PlanEntry* list;
 
-  __device__ __forceinline__ void get(int j, int& kb, uint64_t& m0, uint64_t& m1) const {
+  __device__ __forceinline__ void get(int j, int& kb, int& kb1, uint64_t& m0,
+                                      uint64_t& m1) const {
     if (mode == 0) {
       kb = (j < nsb) ? j : band_start + (j - nsb);
+      kb1 = kb;
       m0 = ~0ull;
       m1 = ~0ull;
     } else {
       const PlanEntry e = list[j];
       kb = e.kb;
+      kb1 = e.kb1;
       m0 = e.m0;
       m1 = e.m1;
     }

@@ -206,7 +206,7 @@ __global__ void __launch_bounds__(128) bs_plan_kernel(const int64_t* idx, int H,
       const int pos = count + __popc(any & ((1u << lane) - 1u));
       PlanEntry e;
       e.kb = kb;
-      e.pad = 0;
+      e.kb1 = kb;
       e.m0 = s0 ? ~0ull : 0ull;
       e.m1 = s1 ? ~0ull : 0ull;
       out[pos] = e;
@@ -214,6 +214,73 @@ __global__ void __launch_bounds__(128) bs_plan_kernel(const int64_t* idx, int H,
     count += __popc(any);
   }
   if (lane == 0) plan_count[(long long)bh * T + t] = count;
+}
+
+// ---------------------------------------------------------------------------
+// Split plan: entry i of tile t pairs the i-th selected key block of query
+// block 2t (rows [0,64) of the tile) with the i-th of query block 2t+1 (rows
+// [64,128)); each half's list is ascending, restricted to kb <= bq.  The
+// tile has max(n0, n1) entries instead of |union|.  A half whose list is
+// shorter gets key block 0 with mask 0 (a valid block, so V holds finite
+// values where P is 0).  One warp per tile.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) bs_split_plan_kernel(const int64_t* idx, int H, int nbq,
+                                                            int nbk, int topk, int T, long long cap,
+                                                            long long head_stride,
+                                                            PlanEntry* plan, int* plan_count) {
+  __shared__ uint32_t bits[4][2][kMaxBlocks / 32];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 4 + w;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int bh = b * H + h;
+  if (t >= T) return;
+  const int hi = min(2 * t + 1, nbk - 1);
+  const int nwords = hi / 32 + 1;
+  for (int i = lane; i < nwords; i += 32) {
+    bits[w][0][i] = 0;
+    bits[w][1][i] = 0;
+  }
+  __syncwarp();
+  for (int half = 0; half < 2; ++half) {
+    const int bq = 2 * t + half;
+    if (bq >= nbq) break;
+    const int64_t* lst = idx + ((long long)bh * nbq + bq) * topk;
+    for (int i = lane; i < topk; i += 32) {
+      const long long kb = lst[i];
+      if (kb >= 0 && kb <= bq && kb <= hi) atomicOr(&bits[w][half][kb >> 5], 1u << (kb & 31));
+    }
+  }
+  __syncwarp();
+  PlanEntry* out = plan + (long long)bh * head_stride + plan_offset(t, cap);
+  int count[2] = {0, 0};
+  for (int half = 0; half < 2; ++half) {
+    for (int base = 0; base <= hi; base += 32) {
+      const int kb = base + lane;
+      const bool sel = (kb <= hi) && ((bits[w][half][base >> 5] >> lane) & 1u);
+      const unsigned any = __ballot_sync(0xffffffffu, sel);
+      if (sel) {
+        PlanEntry* e = out + count[half] + __popc(any & ((1u << lane) - 1u));
+        if (half == 0) {
+          e->kb = kb;
+          e->m0 = ~0ull;
+        } else {
+          e->kb1 = kb;
+          e->m1 = ~0ull;
+        }
+      }
+      count[half] += __popc(any);
+    }
+  }
+  const int n = max(count[0], count[1]);
+  for (int i = count[0] + lane; i < n; i += 32) {
+    out[i].kb = 0;
+    out[i].m0 = 0ull;
+  }
+  for (int i = count[1] + lane; i < n; i += 32) {
+    out[i].kb1 = 0;
+    out[i].m1 = 0ull;
+  }
+  if (lane == 0) plan_count[(long long)bh * T + t] = n;
 }
 
 // ---------------------------------------------------------------------------
@@ -317,8 +384,19 @@ extern "C" int mi_block_sparse_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_
   int* count = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) +
                                       align_up(sizeof(PlanEntry) * B * H * head_stride));
   dim3 g((unsigned)((T + 3) / 4), (unsigned)H, (unsigned)B);
-  bs_plan_kernel<<<g, 128, 0, st>>>(block_idx, (int)H, (int)nb, (int)nb, (int)topk, (int)T, cap,
-                                    head_stride, plan, count);
+  // Split tiles (default): each 64-row query block walks its own list.
+  // MI_BS_SPLIT=0 selects union tiles (both halves walk the union of the
+  // two lists), kept for comparison.
+  static const bool split = [] {
+    const char* e = getenv("MI_BS_SPLIT");
+    return !(e && e[0] == '0');
+  }();
+  if (split)
+    bs_split_plan_kernel<<<g, 128, 0, st>>>(block_idx, (int)H, (int)nb, (int)nb, (int)topk,
+                                            (int)T, cap, head_stride, plan, count);
+  else
+    bs_plan_kernel<<<g, 128, 0, st>>>(block_idx, (int)H, (int)nb, (int)nb, (int)topk, (int)T,
+                                      cap, head_stride, plan, count);
   if (cudaGetLastError() != cudaSuccess) return MI_ERR_LAUNCH;
   AttnParams prm{};
   prm.B = (int)B;
@@ -335,5 +413,6 @@ extern "C" int mi_block_sparse_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_
   prm.plan_count = count;
   prm.plan_cap = cap;
   prm.plan_head_stride = head_stride;
+  prm.split = split ? 1 : 0;
   return launch_attention(q, k, v, out, D, dtype, prm, st);
 }

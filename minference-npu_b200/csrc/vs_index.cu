@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(128) vs_plan_kernel(int H, int S, int nb, int 
     if (keep) {
       PlanEntry e;
       e.kb = kb;
-      e.pad = 0;
+      e.kb1 = kb;
       e.m0 = m0;
       e.m1 = m1;
       out[count + __popc(bal & ((1u << lane) - 1u))] = e;
