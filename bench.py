@@ -51,10 +51,28 @@ def dense_causal_flops(S: int, H: int, d: int = D) -> float:
     return 4.0 * d * H * S * (S + 1) / 2.0
 
 
-def shard_groups(rank: int, world: int, pattern: str = "mixed", n_heads: int = H_TOTAL):
+PATTERN_KEYS = {"vertical_and_slash": ("vertical_and_slash", VS_V, VS_S),
+                "block_sparse": ("block_sparse", BS_TOPK, 0),
+                "stream_llm": ("stream_llm", ST_INIT, ST_LOCAL), "dense": ("dense", 0, 0)}
+
+
+def head_map_for(world: int, pattern: str, n_heads: int, kind: str, S: int):
+    """Heads of every rank: contiguous ranges, or the cost-balanced map of
+    minference.sharding (equal head counts per rank)."""
+    per = n_heads // world
+    if kind == "contiguous" or world == 1:
+        return [list(range(r * per, (r + 1) * per)) for r in range(world)]
+    from minference.sharding import balanced_head_map, head_cost
+
+    pats = head_patterns(n_heads) if pattern == "mixed" else [pattern] * n_heads
+    return balanced_head_map([head_cost(PATTERN_KEYS[p], S) for p in pats], world)
+
+
+def shard_groups(rank: int, world: int, pattern: str = "mixed", n_heads: int = H_TOTAL,
+                 head_map=None):
     """This rank's heads, grouped by pattern: [(pattern, [global heads])]."""
     per = n_heads // world
-    heads = list(range(rank * per, (rank + 1) * per))
+    heads = head_map[rank] if head_map is not None else list(range(rank * per, (rank + 1) * per))
     pats = head_patterns(n_heads) if pattern == "mixed" else [pattern] * n_heads
     groups = []
     for p in ("vertical_and_slash", "block_sparse", "stream_llm", "dense"):
@@ -198,13 +216,13 @@ class ClockSampler:
 class Layer:
     """One rank's share of the layer: inputs resident on the device."""
 
-    def __init__(self, rank, world, S, device, pattern="mixed", n_heads=H_TOTAL):
+    def __init__(self, rank, world, S, device, pattern="mixed", n_heads=H_TOTAL, head_map=None):
         from minference import ops
 
         self.ops = ops
         self.S = S
         self.device = device
-        self.groups = shard_groups(rank, world, pattern, n_heads)
+        self.groups = shard_groups(rank, world, pattern, n_heads, head_map)
         self.heads = [h for _, hs in self.groups for h in hs]
         self.q, self.k, self.v = make_inputs(self.heads, S, device)
         # output stored [B, S, H_rank, D] (what o_proj consumes), written through a BNSD view
@@ -569,6 +587,8 @@ def main():
     ap.add_argument("--ctx", default="4096,8192,16384,32768,65536")
     ap.add_argument("--attn-types", default="minference,dense,hf")
     ap.add_argument("--ttft-runs", type=int, default=2)
+    ap.add_argument("--head-map", default="balanced", choices=["balanced", "contiguous"],
+                    help="head -> rank map for N>1 (minference.sharding)")
     ap.add_argument("--baseline-configs", action="store_true",
                     help="BASELINE configs 0-2 as single-layer ops (one JSON line each)")
     args = ap.parse_args()
@@ -604,7 +624,8 @@ def main():
     from minference import _native
 
     S = args.seq
-    layer = Layer(rank, world, S, device, args.pattern, args.heads)
+    head_map = head_map_for(world, args.pattern, args.heads, args.head_map, S)
+    layer = Layer(rank, world, S, device, args.pattern, args.heads, head_map)
     n_heads = args.heads
     gathered = None
     if world > 1:
@@ -716,6 +737,7 @@ def main():
                        "model": "Phi-3-mini-128k attention shape", "global_batch": 1, "seq_len": S,
                        "heads": n_heads, "head_dim": D, "pattern": args.pattern,
                        "parallelism": f"head-shard{world}" if world > 1 else "single",
+                       "head_map": args.head_map if world > 1 else "single",
                        "l2": "inputs 1.2 GB > L2 (no flush needed)"},
             "ms_per_layer": ms,
             "dense_ms_per_layer": dense_ms,

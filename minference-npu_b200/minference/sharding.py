@@ -1,10 +1,18 @@
 """Head-sharded execution across GPUs (one process per GPU).
 
 Every MInference pattern is independent per head, index estimation
-included, so a layer's heads split contiguously over the ranks with no
-exchange during attention.  The only exchange is re-assembling the head
-outputs for ``o_proj``: an all-gather of each rank's ``[B, S, H/G, D]``
-slice (NCCL over NVLink/NVSwitch on B200; gloo works for CPU tests).
+included, so a layer's heads split over the ranks with no exchange during
+attention.  The only exchange is re-assembling the head outputs for
+``o_proj``: an all-gather of each rank's ``[B, S, h_r, D]`` slice (NCCL over
+NVLink/NVSwitch on B200; gloo works for CPU tests).
+
+Two head maps:
+  * contiguous (`head_range`): rank r takes a contiguous range;
+  * cost-balanced (`balanced_head_map`): per-head costs from the pattern
+    config (`head_cost`), assigned longest-first to the least-loaded rank
+    with equal head counts per rank, so the layer time (set by the slowest
+    rank) drops when the pattern mix is uneven across contiguous ranges.
+    `gather_heads_mapped` re-assembles head order after the all-gather.
 """
 
 from __future__ import annotations
@@ -12,7 +20,8 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-__all__ = ["head_range", "gather_heads"]
+__all__ = ["head_range", "gather_heads", "head_cost", "balanced_head_map",
+           "gather_heads_mapped", "o_proj_input_permutation"]
 
 
 def head_range(num_heads: int, rank: int, world: int) -> range:
@@ -50,3 +59,78 @@ def gather_heads(local_bshd: torch.Tensor, num_heads: int, group=None) -> torch.
         dist.all_gather(parts, x, group=group)
     parts = [p[:, :, : sizes[r]] for r, p in enumerate(parts)]
     return torch.cat(parts, dim=2)
+
+
+def head_cost(pattern, S: int) -> float:
+    """Relative attention cost of one head: its visible (query, key) pairs.
+
+    pattern: (type, v, s[, score]) as in the pattern JSON.  vertical_and_slash
+    and dense count the causal triangle (at long contexts the VS set covers
+    nearly all of it); block_sparse counts its selected 64x64 blocks;
+    stream_llm counts sink plus window keys per query."""
+    ty = pattern[0]
+    causal = S * (S + 1) / 2.0
+    if ty == "block_sparse":
+        return min(causal, float(S) * 64.0 * max(1, int(pattern[1])))
+    if ty == "stream_llm":
+        return min(causal, float(S) * (int(pattern[1]) + int(pattern[2])))
+    if ty in ("vertical_and_slash", "dense"):
+        return causal
+    raise ValueError(f"unknown pattern type {ty!r}")
+
+
+def balanced_head_map(costs, world: int) -> list[list[int]]:
+    """Heads per rank, each list ascending.  Requires len(costs) % world == 0
+    (every rank holds the same number of heads, which keeps the fused
+    equal-size all-gather).  Longest-processing-time-first: heads in
+    decreasing cost go to the least-loaded rank that still has room; ties go
+    to the lower rank, so the map is deterministic."""
+    n = len(costs)
+    if world <= 0 or n % world:
+        raise ValueError(f"{n} heads do not split evenly over {world} ranks")
+    per = n // world
+    load = [0.0] * world
+    ranks: list[list[int]] = [[] for _ in range(world)]
+    for h in sorted(range(n), key=lambda i: (-costs[i], i)):
+        r = min((r for r in range(world) if len(ranks[r]) < per), key=lambda r: (load[r], r))
+        ranks[r].append(h)
+        load[r] += costs[h]
+    return [sorted(hs) for hs in ranks]
+
+
+def gather_heads_mapped(local_bshd: torch.Tensor, head_map: list[list[int]],
+                        group=None) -> torch.Tensor:
+    """All-gather ``[B, S, h, D]`` slices whose heads are ``head_map[rank]``
+    (equal sizes) and return ``[B, S, H, D]`` in global head order."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    if len(head_map) != world:
+        raise ValueError(f"head map has {len(head_map)} ranks, group has {world}")
+    B, S, h_local, D = local_bshd.shape
+    if len(head_map[rank]) != h_local:
+        raise ValueError(f"rank {rank} holds {h_local} heads, map says {len(head_map[rank])}")
+    x = local_bshd.contiguous()
+    if dist.get_backend(group) == "nccl":
+        buf = torch.empty((world,) + tuple(x.shape), dtype=x.dtype, device=x.device)
+        dist.all_gather_into_tensor(buf, x, group=group)
+        parts = list(buf.unbind(0))
+    else:
+        parts = [torch.empty_like(x) for _ in range(world)]
+        dist.all_gather(parts, x, group=group)
+    order = [h for hs in head_map for h in hs]  # head held at each gathered position
+    inv = torch.empty(len(order), dtype=torch.long)
+    inv[torch.tensor(order)] = torch.arange(len(order))
+    return torch.cat(parts, dim=2).index_select(2, inv.to(x.device))
+
+
+def o_proj_input_permutation(head_map: list[list[int]], head_dim: int) -> torch.Tensor:
+    """Column order for o_proj's weight that consumes the rank-major gathered
+    layout directly.
+
+    After ``all_gather_into_tensor`` of equal slices, feature f of the
+    gathered ``[B, S, H*D]`` row holds global feature perm[f].  Multiplying
+    by ``W[:, perm]`` (permuted once, at load time) equals multiplying the
+    head-ordered activations by W, so no per-layer re-ordering copy is needed."""
+    order = [h for hs in head_map for h in hs]
+    return torch.tensor([h * head_dim + d for h in order for d in range(head_dim)],
+                        dtype=torch.long)

@@ -76,3 +76,66 @@ def test_head_range_partition():
             assert heads == list(range(H))
     with pytest.raises(ValueError):
         head_range(32, 2, 2)
+
+
+def test_balanced_head_map_properties():
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "minference-npu_b200"))
+    from minference.sharding import balanced_head_map, head_cost
+
+    cycle = [("vertical_and_slash", 1000, 6096), ("block_sparse", 100, 0),
+             ("vertical_and_slash", 1000, 6096), ("block_sparse", 100, 0), ("stream_llm", 128, 1024)]
+    pats = [cycle[h % 5] for h in range(32)]
+    costs = [head_cost(p, 65536) for p in pats]
+    for world in (1, 2, 4, 8):
+        m = balanced_head_map(costs, world)
+        assert sorted(h for hs in m for h in hs) == list(range(32))
+        assert all(len(hs) == 32 // world for hs in m)
+        assert m == balanced_head_map(costs, world)  # deterministic
+        bal = max(sum(costs[h] for h in hs) for hs in m)
+        contig = max(sum(costs[h] for h in range(r * 32 // world, (r + 1) * 32 // world))
+                     for r in range(world))
+        assert bal <= contig + 1e-6
+    # 8 ranks: the contiguous map puts 2 VS + 2 block_sparse heads on some ranks
+    m8 = balanced_head_map(costs, 8)
+    assert max(sum(costs[h] for h in hs) for hs in m8) < contig
+    with pytest.raises(ValueError):
+        balanced_head_map(costs[:5], 2)
+
+
+def _worker_mapped(rank, world, port, head_map, q):
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "minference-npu_b200"))
+    import torch.distributed as dist
+
+    from minference.sharding import gather_heads_mapped
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        n = sum(len(hs) for hs in head_map)
+        local = torch.stack([_head_output(h) for h in head_map[rank]], dim=2)
+        full = gather_heads_mapped(local, head_map)
+        want = torch.stack([_head_output(h) for h in range(n)], dim=2)
+        q.put((rank, bool(torch.equal(full, want)), head_map[rank]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_heads_mapped_gloo():
+    head_map = [[0, 3, 5, 6], [1, 2, 4, 7]]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_mapped, args=(r, 2, port, head_map, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(ok for _, ok, _ in res), res
