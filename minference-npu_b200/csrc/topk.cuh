@@ -1,23 +1,20 @@
 // Block-wide exact top-k selection with lowest-index tie-break.
 //
 // Keys are order-preserving uint32 images of fp32 scores (float_to_ordered).
-// The k-th largest key is found by a 4-pass 8-bit radix select over
-// shared-memory histograms; the result set is then {key > T} plus the first
-// `need` elements equal to T in index order, emitted in ascending index order
-// via two block-wide exclusive scans.  Each thread owns a contiguous chunk of
-// indices, so "index order" is (thread, position in chunk).
+// The k-th largest key T is found by a 4-pass 8-bit radix select; the result
+// set is then {key > T} plus the first `need` elements equal to T in index
+// order, emitted in ascending index order.
+//
+// Warp w owns the contiguous index segment [w*seg, (w+1)*seg) and walks it
+// in rounds of 32 consecutive indices, so every load is coalesced and index
+// order inside a round comes from ballots.  Histograms are per warp, and
+// lanes holding the same digit in a round are merged with __match_any_sync
+// into one add: the scores' leading bytes are shared by most keys, so a
+// block-wide histogram would serialise on one or two bins.
 #pragma once
 #include "common.cuh"
 
 namespace mib200 {
-
-template <int NT>
-struct TopkSmem {
-  int hist[256];
-  int warp_tot[NT / 32];
-  int sel_digit;
-  int remaining;
-};
 
 // Exclusive block scan of one int per thread; returns the exclusive prefix,
 // writes the block total to *total.
@@ -44,26 +41,56 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot, int* t
   return base + x - v;
 }
 
+template <int NT>
+struct TopkSmem {
+  int hist[NT / 32][256];  // per-warp digit histograms
+  int tot[256];
+  int warp_cnt[NT / 32];
+  int sel_digit;
+  int remaining;
+};
+
+// Sum of warp_cnt[0..w) for the calling warp (after a block barrier).
+template <int NT>
+__device__ __forceinline__ int warps_before(const int* warp_cnt, int w) {
+  int s = 0;
+  for (int x = 0; x < w; ++x) s += warp_cnt[x];
+  return s;
+}
+
 // keys: n entries (shared or global memory).  Calls emit(pos, index) for the
 // k selected indices with pos = 0..k-1 in ascending index order.
 template <int NT, typename Emit>
 __device__ void block_topk(const uint32_t* keys, int n, int k, TopkSmem<NT>& sm, Emit emit) {
+  constexpr int NW = NT / 32;
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
-  const int ept = (n + NT - 1) / NT;
-  const int beg = min(n, tid * ept);
-  const int end = min(n, beg + ept);
+  const unsigned lt = (1u << lane) - 1u;
   if (k <= 0) return;
   if (k > n) k = n;
+  const int seg = (((n + NW - 1) / NW) + 31) & ~31;
+  const int wbeg = min(n, warp * seg);
+  const int wend = min(n, wbeg + seg);
 
   uint32_t prefix = 0, pmask = 0;
   if (tid == 0) sm.remaining = k;
   for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = tid; i < 256; i += NT) sm.hist[i] = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) sm.hist[warp][lane * 8 + q] = 0;
+    __syncwarp();
+    for (int base = wbeg; base < wend; base += 32) {
+      const int i = base + lane;
+      const uint32_t key = i < wend ? keys[i] : 0u;
+      const int d = (i < wend && (key & pmask) == prefix) ? (int)((key >> shift) & 255) : 256;
+      const unsigned same = __match_any_sync(0xffffffffu, d);
+      if (d != 256 && lane == __ffs(same) - 1) atomicAdd(&sm.hist[warp][d], __popc(same));
+    }
     __syncthreads();
-    for (int i = beg; i < end; ++i) {
-      const uint32_t key = keys[i];
-      if ((key & pmask) == prefix) atomicAdd(&sm.hist[(key >> shift) & 255], 1);
+    for (int b = tid; b < 256; b += NT) {
+      int c = 0;
+#pragma unroll 8
+      for (int w = 0; w < NW; ++w) c += sm.hist[w][b];
+      sm.tot[b] = c;
     }
     __syncthreads();
     if (warp == 0) {
@@ -72,7 +99,7 @@ __device__ void block_topk(const uint32_t* keys, int n, int k, TopkSmem<NT>& sm,
       int s = 0;
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        c[q] = sm.hist[255 - 8 * lane - q];
+        c[q] = sm.tot[255 - 8 * lane - q];
         s += c[q];
       }
       int incl = s;
@@ -101,43 +128,44 @@ __device__ void block_topk(const uint32_t* keys, int n, int k, TopkSmem<NT>& sm,
     __syncthreads();
     prefix |= (uint32_t)sm.sel_digit << shift;
     pmask |= 255u << shift;
-    __syncthreads();
   }
   const uint32_t T = prefix;
   const int need_eq = sm.remaining;
 
-  int eq_local = 0;
-  for (int i = beg; i < end; ++i) eq_local += (keys[i] == T);
-  int tot;
-  const int eq_before = block_exclusive_scan<NT>(eq_local, sm.warp_tot, &tot);
-  int sel_local = 0;
-  {
-    int eq_seen = eq_before;
-    for (int i = beg; i < end; ++i) {
-      const uint32_t key = keys[i];
-      if (key > T) {
-        ++sel_local;
-      } else if (key == T) {
-        if (eq_seen < need_eq) ++sel_local;
-        ++eq_seen;
-      }
-    }
+  // Elements equal to T before this warp's segment.
+  int eq_w = 0;
+  for (int base = wbeg; base < wend; base += 32) {
+    const int i = base + lane;
+    eq_w += __popc(__ballot_sync(0xffffffffu, i < wend && keys[i] == T));
   }
-  const int pos0 = block_exclusive_scan<NT>(sel_local, sm.warp_tot, &tot);
-  int pos = pos0;
-  int eq_seen = eq_before;
-  for (int i = beg; i < end; ++i) {
-    const uint32_t key = keys[i];
-    bool sel = false;
-    if (key > T) {
-      sel = true;
-    } else if (key == T) {
-      sel = eq_seen < need_eq;
-      ++eq_seen;
+  if (lane == 0) sm.warp_cnt[warp] = eq_w;
+  __syncthreads();
+  const int eq_before = warps_before<NT>(sm.warp_cnt, warp);
+  __syncthreads();
+  // Walks the segment; calls f(i, rank in the selection among this warp's
+  // selected elements) for selected i.  Returns the warp's selected count.
+  auto walk = [&](auto&& f) -> int {
+    int eq_seen = eq_before, cnt = 0;
+    for (int base = wbeg; base < wend; base += 32) {
+      const int i = base + lane;
+      const bool valid = i < wend;
+      const uint32_t key = valid ? keys[i] : 0u;
+      const bool eq = valid && key == T;
+      const unsigned eqb = __ballot_sync(0xffffffffu, eq);
+      const bool sel = valid && (key > T || (eq && eq_seen + __popc(eqb & lt) < need_eq));
+      const unsigned selb = __ballot_sync(0xffffffffu, sel);
+      if (sel) f(i, cnt + __popc(selb & lt));
+      cnt += __popc(selb);
+      eq_seen += __popc(eqb);
     }
-    if (sel) emit(pos++, i);
-  }
-  (void)lane;
+    return cnt;
+  };
+  const int sel_w = walk([](int, int) {});
+  if (lane == 0) sm.warp_cnt[warp] = sel_w;
+  __syncthreads();
+  const int pos_base = warps_before<NT>(sm.warp_cnt, warp);
+  walk([&](int i, int r) { emit(pos_base + r, i); });
+  __syncthreads();
 }
 
 // Warp-scope variant: the calling warp selects k of n keys on its own (no
