@@ -473,12 +473,18 @@ static int launch_attn_t(const mi_tensor4& q, const mi_tensor4& k, const mi_tens
   if ((rc = make_bnsd_map(&to, out, prm.B, prm.H, prm.Sq, D, 32, kBM)) != MI_OK) return rc;
   auto kern = attn_fwd_kernel<DT, D, SPLIT>;
   const int alloc = L::kAlloc;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, alloc) !=
-      cudaSuccess)
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, alloc);
+  if (e == cudaSuccess) {
+    dim3 grid(prm.T, prm.H, prm.B);
+    kern<<<grid, kThreads, alloc, stream>>>(tq, tk, tv, to, prm);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) {
+    debug_launch_failure("attn_fwd_kernel", reinterpret_cast<const void*>(kern), e, kThreads,
+                         alloc);
     return MI_ERR_LAUNCH;
-  dim3 grid(prm.T, prm.H, prm.B);
-  kern<<<grid, kThreads, alloc, stream>>>(tq, tk, tv, to, prm);
-  return cudaGetLastError() == cudaSuccess ? MI_OK : MI_ERR_LAUNCH;
+  }
+  return MI_OK;
 }
 
 int launch_attention(const mi_tensor4& q, const mi_tensor4& k, const mi_tensor4& v,

@@ -4,6 +4,8 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <cstdio>
+#include <cstdlib>
 
 #include "../../include/minference_b200.h"
 
@@ -53,6 +55,22 @@ inline int make_bnsd_map(CUtensorMap* map, const mi_tensor4& t, int64_t B, int64
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? MI_OK : MI_ERR_ALIGN;
+}
+
+// With MI_DEBUG=1 in the environment, a failed kernel launch prints the CUDA
+// error and the kernel's resource attributes to stderr (the C ABI itself only
+// returns MI_ERR_LAUNCH).
+inline void debug_launch_failure(const char* name, const void* func, cudaError_t err,
+                                 int threads, int smem_bytes) {
+  const char* dbg = getenv("MI_DEBUG");
+  if (!dbg || dbg[0] != '1') return;
+  cudaFuncAttributes fa{};
+  cudaFuncGetAttributes(&fa, func);
+  fprintf(stderr,
+          "[minference_b200] %s launch failed: %s (threads %d, dynamic smem %d; kernel: %d regs, "
+          "max threads %d, static smem %zu, local %zu)\n",
+          name, cudaGetErrorString(err), threads, smem_bytes, fa.numRegs, fa.maxThreadsPerBlock,
+          fa.sharedSizeBytes, fa.localSizeBytes);
 }
 
 }  // namespace mib200
