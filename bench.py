@@ -587,6 +587,9 @@ def main():
     ap.add_argument("--ctx", default="4096,8192,16384,32768,65536")
     ap.add_argument("--attn-types", default="minference,dense,hf")
     ap.add_argument("--ttft-runs", type=int, default=2)
+    ap.add_argument("--o-proj", default="none", choices=["none", "serial", "overlap"],
+                    help="N>1: follow the all-gather with Phi-3's o_proj GEMM, either after "
+                         "the whole gather (serial) or chunk by chunk behind it (overlap)")
     ap.add_argument("--head-map", default="balanced", choices=["balanced", "contiguous"],
                     help="head -> rank map for N>1 (minference.sharding)")
     ap.add_argument("--baseline-configs", action="store_true",
@@ -632,10 +635,28 @@ def main():
         gathered = torch.empty((world,) + tuple(layer.out_bshd.shape), dtype=torch.bfloat16,
                                device=device)
 
+    w_oproj = None
+    if world > 1 and args.o_proj != "none":
+        from minference.sharding import o_proj_input_permutation
+
+        g = torch.Generator(device=device).manual_seed(77)
+        w = torch.randn(n_heads * D, n_heads * D, generator=g, device=device) / math.sqrt(n_heads * D)
+        w_oproj = w.to(torch.bfloat16)[:, o_proj_input_permutation(head_map, D).to(device)]
+
     def step(q=None, k=None, v=None, ev=None):
         o = layer.run(q, k, v, ev)
         if world > 1:
+            if args.o_proj == "overlap":
+                from minference.sharding import gather_o_proj
+
+                return gather_o_proj(o, w_oproj, chunks=4)
             torch.distributed.all_gather_into_tensor(gathered, o)
+            if args.o_proj == "serial":  # the same per-rank GEMMs, after the whole gather
+                hd = o.shape[2] * D
+                acc = torch.matmul(gathered[0].reshape(S, hd), w_oproj[:, :hd].t())
+                for r in range(1, world):
+                    acc.addmm_(gathered[r].reshape(S, hd), w_oproj[:, r * hd:(r + 1) * hd].t())
+                return acc.view(1, S, n_heads * D)
         return o
 
     def barrier():
@@ -652,8 +673,9 @@ def main():
 
     # ---- warmup + algorithmic work -----------------------------------------------
     for _ in range(args.warmup):
-        step()
+        o_last = step()
     torch.cuda.synchronize()
+    out_shape = tuple(o_last.shape)
     vis_pairs = layer.visible_pairs()
     alg_flops_rank = 4.0 * D * vis_pairs
 
@@ -681,7 +703,7 @@ def main():
     pin_q = layer.q.cpu().pin_memory()
     pin_k = layer.k.cpu().pin_memory()
     pin_v = layer.v.cpu().pin_memory()
-    pin_o = torch.empty(layer.out_bshd.shape, dtype=torch.bfloat16).pin_memory()
+    pin_o = torch.empty(out_shape, dtype=torch.bfloat16).pin_memory()
     dq, dk_, dv = torch.empty_like(layer.q), torch.empty_like(layer.k), torch.empty_like(layer.v)
     e_steps = max(2, min(args.steps, 5))
     barrier()
@@ -698,7 +720,7 @@ def main():
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e_steps)
     h2d = 3 * layer.q.numel() * 2
-    d2h = layer.out_bshd.numel() * 2
+    d2h = math.prod(out_shape) * 2
 
     # ---- dense comparator (same heads, dense causal with the same kernel) --------
     barrier()
@@ -738,6 +760,7 @@ def main():
                        "heads": n_heads, "head_dim": D, "pattern": args.pattern,
                        "parallelism": f"head-shard{world}" if world > 1 else "single",
                        "head_map": args.head_map if world > 1 else "single",
+                       "o_proj": args.o_proj if world > 1 else "none",
                        "l2": "inputs 1.2 GB > L2 (no flush needed)"},
             "ms_per_layer": ms,
             "dense_ms_per_layer": dense_ms,

@@ -21,7 +21,7 @@ import torch
 import torch.distributed as dist
 
 __all__ = ["head_range", "gather_heads", "head_cost", "balanced_head_map",
-           "gather_heads_mapped", "o_proj_input_permutation"]
+           "gather_heads_mapped", "o_proj_input_permutation", "gather_o_proj"]
 
 
 def head_range(num_heads: int, rank: int, world: int) -> range:
@@ -134,3 +134,88 @@ def o_proj_input_permutation(head_map: list[list[int]], head_dim: int) -> torch.
     order = [h for hs in head_map for h in hs]
     return torch.tensor([h * head_dim + d for h in order for d in range(head_dim)],
                         dtype=torch.long)
+
+
+_comm_streams: dict[int, torch.cuda.Stream] = {}
+_gather_bufs: dict[tuple, list[torch.Tensor]] = {}
+
+
+def _comm_stream(device: torch.device) -> torch.cuda.Stream:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _comm_streams:
+        _comm_streams[idx] = torch.cuda.Stream(device=idx)
+    return _comm_streams[idx]
+
+
+def gather_o_proj(local_bshd: torch.Tensor, weight_perm: torch.Tensor, bias=None, group=None,
+                  chunks: int = 4) -> torch.Tensor:
+    """o_proj of the all-gathered heads, with the gather overlapped.
+
+    local_bshd: this rank's ``[B, S, h, D]`` head outputs (equal h on every
+    rank).  weight_perm: o_proj's ``[hidden, H*D]`` weight with its input
+    columns permuted by `o_proj_input_permutation` for the head map in use,
+    so that rank r's slice of the gathered layout multiplies the column block
+    ``weight_perm[:, r*h*D:(r+1)*h*D]``.  Returns ``[B, S, hidden]``, the same
+    on every rank.
+
+    The sequence is cut into `chunks` pieces.  With NCCL, the all-gather of
+    piece c+1 runs on a side stream while the GEMMs of piece c run on the
+    current stream, so the transfer hides behind o_proj.  Each piece's output
+    is accumulated rank by rank (one addmm per rank) straight from the gather
+    buffer, with no re-ordering copy.  The gather buffers are cached per
+    shape and reused by the next call; calls on one device must not overlap.
+    Other backends (gloo on CPU) run the pieces one after another."""
+    world = dist.get_world_size(group)
+    B, S, h, D = local_bshd.shape
+    hd = h * D
+    hidden = weight_perm.shape[0]
+    x = local_bshd.contiguous()
+    bounds = [S * i // chunks for i in range(chunks + 1)]
+    out = torch.empty((B, S, hidden), dtype=x.dtype, device=x.device)
+    wt = [weight_perm[:, r * hd:(r + 1) * hd].t() for r in range(world)]
+
+    def project(parts, lo, hi):
+        # out[:, lo:hi] = sum_r parts[r] @ W_r^T (+ bias)
+        rows = B * (hi - lo)
+        dst = out[:, lo:hi]
+        acc = dst.reshape(rows, hidden) if B == 1 else torch.empty(rows, hidden, dtype=x.dtype,
+                                                                     device=x.device)
+        torch.matmul(parts[0].reshape(rows, hd), wt[0], out=acc)
+        for r in range(1, world):
+            acc.addmm_(parts[r].reshape(rows, hd), wt[r])
+        if bias is not None:
+            acc.add_(bias)
+        if B != 1:
+            dst.copy_(acc.view(B, hi - lo, hidden))
+
+    nccl = dist.get_backend(group) == "nccl" and x.is_cuda
+    if not nccl:
+        for c in range(chunks):
+            lo, hi = bounds[c], bounds[c + 1]
+            piece = x[:, lo:hi].contiguous()
+            parts = [torch.empty_like(piece) for _ in range(world)]
+            dist.all_gather(parts, piece, group=group)
+            project(parts, lo, hi)
+        return out
+    main = torch.cuda.current_stream(x.device)
+    comm = _comm_stream(x.device)
+    key = (x.device, world, B, S, h, D, x.dtype, chunks)
+    if key not in _gather_bufs:
+        _gather_bufs[key] = [torch.empty((world, B, bounds[c + 1] - bounds[c], h, D), dtype=x.dtype,
+                                         device=x.device) for c in range(chunks)]
+    bufs = _gather_bufs[key]
+    # x is ready, and the previous call's GEMMs (which read bufs) have run.
+    comm.wait_stream(main)
+    events = []
+    with torch.cuda.stream(comm):
+        for c in range(chunks):
+            lo, hi = bounds[c], bounds[c + 1]
+            dist.all_gather_into_tensor(bufs[c], x[:, lo:hi].contiguous(), group=group)
+            e = torch.cuda.Event()
+            e.record(comm)
+            events.append(e)
+    for c in range(chunks):
+        main.wait_event(events[c])
+        project(bufs[c].unbind(0), bounds[c], bounds[c + 1])
+    x.record_stream(comm)
+    return out

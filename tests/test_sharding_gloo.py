@@ -139,3 +139,47 @@ def test_gather_heads_mapped_gloo():
     for p in procs:
         p.join(timeout=60)
     assert all(ok for _, ok, _ in res), res
+
+
+def _worker_oproj(rank, world, port, q):
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "minference-npu_b200"))
+    import torch.distributed as dist
+
+    from minference.sharding import gather_o_proj, o_proj_input_permutation
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        head_map = [[0, 3, 5, 6], [1, 2, 4, 7]]
+        D, hidden = 8, 12
+        g = torch.Generator().manual_seed(7)
+        W = torch.randn(hidden, 8 * D, generator=g, dtype=torch.float64)
+        bias = torch.randn(hidden, generator=g, dtype=torch.float64)
+        heads = [_head_output(h).double() for h in range(8)]  # [B, S, D] each
+        local = torch.stack([heads[h] for h in head_map[rank]], dim=2)
+        wp = W[:, o_proj_input_permutation(head_map, D)]
+        got = gather_o_proj(local, wp, bias, chunks=3)
+        full = torch.stack(heads, dim=2).reshape(1, 16, 8 * D)  # head order
+        want = full @ W.T + bias
+        q.put((rank, bool(torch.allclose(got, want, atol=1e-10)), None))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_o_proj_gloo():
+    """Chunked gather + o_proj with a permuted weight equals o_proj of the
+    head-ordered layer output."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_oproj, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(ok for _, ok, _ in res), res
