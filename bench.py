@@ -297,6 +297,23 @@ class Layer:
         return tot
 
 
+# DRAM read + write bytes per head of one attention launch at S = 65536, D = 96,
+# bf16, from one ncu capture (profiles/attn_dram_traffic_64k.md).
+ATTN_DRAM_BYTES_PER_HEAD_64K = {"vertical_and_slash": 49.4e6, "block_sparse": 42.2e6,
+                                "stream_llm": 37.9e6}
+
+
+def attn_traffic_bytes(layer, S: int):
+    if S != 65536:
+        return None
+    tot = 0.0
+    for p, sl in layer.slices:
+        if p not in ATTN_DRAM_BYTES_PER_HEAD_64K:
+            return None
+        tot += ATTN_DRAM_BYTES_PER_HEAD_64K[p] * (sl.stop - sl.start)
+    return tot
+
+
 def _peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -767,7 +784,11 @@ def main():
             "speedup_vs_dense": dense_ms / ms,
             "attn_phase_ms": attn_ms,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf_peak,
-                         "unit": "TFLOP/s", "frac": achieved / tf_peak, "traffic": None,
+                         "unit": "TFLOP/s", "frac": achieved / tf_peak,
+                         "traffic": attn_traffic_bytes(layer, S),
+                         "traffic_note": "DRAM read+write bytes per step of the attention launches: "
+                                         "ncu per-head figures (profiles/attn_dram_traffic_64k.md) "
+                                         "times this rank's heads per pattern; null off S=65536",
                          "peak_kind": peak_kind,
                          "kernel": "attn_fwd_kernel (+ plan kernels), visible-pair FLOPs 4*D*N_vis",
                          "visible_fraction": vis_pairs / (len(layer.heads) * S * (S + 1) / 2)},
