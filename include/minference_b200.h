@@ -123,7 +123,9 @@ int mi_block_sparse_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor4 out
  * descending (s = S-1-diagonal).  Columns 0..29 and slashes 0..99 are forced
  * in.  `logit_scale` is applied as in the reference (1/sqrt(D)).
  * vertical_size / slash_size must already be clamped by the caller
- * (min(S, max(v, 30)), min(S, max(s, 50))).
+ * (min(S, max(v, 30)), min(S, max(s, 50))).  q and k rows are read with
+ * 16-byte loads: unit dim stride, batch/head/row strides multiples of 8
+ * elements and 16-byte aligned base pointers, else MI_ERR_ALIGN.
  * Replaces _vertical_and_slash_kernel (minference_forward.py:140-167). */
 size_t mi_vs_estimate_workspace_size(int64_t B, int64_t H, int64_t S);
 int mi_vs_estimate(mi_tensor4 q, mi_tensor4 k, int64_t B, int64_t H, int64_t S, int64_t D,

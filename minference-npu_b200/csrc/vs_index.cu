@@ -75,10 +75,30 @@ __global__ void __launch_bounds__(128) vs_logits_kernel(mi_tensor4 q, mi_tensor4
   const int key0 = blockIdx.x * kLgKeys;
   const uint16_t* qb = reinterpret_cast<const uint16_t*>(q.ptr) + (long long)b * q.stride_b +
                        (long long)h * q.stride_h;
-  for (int e = threadIdx.x; e < kLgRows * D; e += blockDim.x) {
-    const int i = e % kLgRows, d = e / kLgRows;
-    qs[d * kLgRows + i] =
-        i < LQ ? DType<DT>::to_f(qb[(long long)(S - LQ + i) * q.stride_s + d]) : 0.f;
+  // Q tile: 16-byte loads (8 dims of one row), all issued before the
+  // transposed fp32 stores; consecutive threads take consecutive rows, so
+  // the stores are conflict-free.
+  {
+    constexpr int kUnits = kLgRows * D / 8;  // (row, 8-dim chunk) pairs
+    constexpr int kPer = (kUnits + 127) / 128;
+    uint4 raw[kPer];
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) {
+      const int e = threadIdx.x + r * 128;
+      const int i = e % kLgRows, dc = e / kLgRows;
+      raw[r] = make_uint4(0u, 0u, 0u, 0u);
+      if (e < kUnits && i < LQ)
+        raw[r] = *reinterpret_cast<const uint4*>(qb + (long long)(S - LQ + i) * q.stride_s + dc * 8);
+    }
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) {
+      const int e = threadIdx.x + r * 128;
+      if (e >= kUnits) break;
+      const int i = e % kLgRows, dc = e / kLgRows;
+      const uint16_t* hv = reinterpret_cast<const uint16_t*>(&raw[r]);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) qs[(dc * 8 + u) * kLgRows + i] = DType<DT>::to_f(hv[u]);
+    }
   }
   {
     const int c = key0 + threadIdx.x;
@@ -419,8 +439,13 @@ extern "C" int mi_vs_estimate(mi_tensor4 q, mi_tensor4 k, int64_t B, int64_t H, 
   if (B < 0 || H < 0 || S < 0 || S > (1 << 24)) return MI_ERR_SHAPE;
   if (vertical_size < 1 || vertical_size > S || slash_size < 1 || slash_size > S)
     return MI_ERR_SHAPE;
-  if (q.stride_d != 1 || k.stride_d != 1 || (k.stride_s % 8) || (reinterpret_cast<uintptr_t>(k.ptr) & 15))
-    return MI_ERR_ALIGN;
+  // Rows of q and k are read with 16-byte loads: unit dim stride, 8-element
+  // (16-byte) aligned batch / head / row strides and base pointers.
+  auto rows16 = [](const mi_tensor4& t) {
+    return t.stride_d == 1 && t.stride_s % 8 == 0 && t.stride_h % 8 == 0 && t.stride_b % 8 == 0 &&
+           (reinterpret_cast<uintptr_t>(t.ptr) & 15) == 0;
+  };
+  if (!rows16(q) || !rows16(k)) return MI_ERR_ALIGN;
   if (B == 0 || H == 0 || S == 0) return MI_OK;
   if (!workspace || workspace_bytes < mi_vs_estimate_workspace_size(B, H, S)) return MI_ERR_WORKSPACE;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
