@@ -177,8 +177,13 @@ __global__ void __launch_bounds__(128) vs_logits_kernel(mi_tensor4 q, mi_tensor4
 // ---------------------------------------------------------------------------
 // K3b: per-row max and sum of exp(x - max) (64-bit fixed point, so the sum is
 // independent of the reduction order).  Grid (LQ, H, B), 1024 threads.
-// stats: [BH][LQ] {m, l}.
+// stats: [BH][LQ] {m, 1/l}.  Rows up to kRowRegs * 8 * 1024 elements are read
+// once with 16-byte loads and kept in registers for both passes (the max and
+// the integer sum do not depend on the order); longer or unaligned rows take
+// the two-pass scalar loop.
 // ---------------------------------------------------------------------------
+constexpr int kRowRegs = 8;  // uint4 per thread: 64 elements, rows up to 65536
+
 template <typename DT>
 __global__ void __launch_bounds__(1024) vs_rowstats_kernel(const uint16_t* x, int H, int S,
                                                            int LQ, float2* stats) {
@@ -186,17 +191,50 @@ __global__ void __launch_bounds__(1024) vs_rowstats_kernel(const uint16_t* x, in
   __shared__ unsigned long long red_s[32];
   const int i = blockIdx.x, h = blockIdx.y, b = blockIdx.z, bh = b * H + h;
   const uint16_t* xr = x + ((long long)bh * LQ + i) * S;
+  const bool vec = S % 8 == 0 && S <= kRowRegs * 8 * 1024 &&
+                   (reinterpret_cast<uintptr_t>(xr) & 15) == 0;
+  uint4 v[kRowRegs];
   float m = -INFINITY;
-  for (int c = threadIdx.x; c < S; c += blockDim.x) m = fmaxf(m, DType<DT>::to_f(xr[c]));
+  if (vec) {
+    const int nv = S / 8;
+#pragma unroll
+    for (int r = 0; r < kRowRegs; ++r) {
+      const int u = threadIdx.x + r * 1024;
+      v[r] = u < nv ? reinterpret_cast<const uint4*>(xr)[u] : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int r = 0; r < kRowRegs; ++r) {
+      if (threadIdx.x + r * 1024 < nv) {
+        const uint16_t* hv = reinterpret_cast<const uint16_t*>(&v[r]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m = fmaxf(m, DType<DT>::to_f(hv[e]));
+      }
+    }
+  } else {
+    for (int c = threadIdx.x; c < S; c += blockDim.x) m = fmaxf(m, DType<DT>::to_f(xr[c]));
+  }
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   if ((threadIdx.x & 31) == 0) red_m[threadIdx.x >> 5] = m;
   __syncthreads();
   m = red_m[0];
   for (int w = 1; w < 32; ++w) m = fmaxf(m, red_m[w]);
   unsigned long long s = 0;
-  for (int c = threadIdx.x; c < S; c += blockDim.x) {
-    const float e = det_exp(__fsub_rn(DType<DT>::to_f(xr[c]), m));
+  auto add = [&](uint16_t bits) {
+    const float e = det_exp(__fsub_rn(DType<DT>::to_f(bits), m));
     s += (unsigned long long)__float2ll_rz((float)(e * (float)kFixScale));
+  };
+  if (vec) {
+    const int nv = S / 8;
+#pragma unroll
+    for (int r = 0; r < kRowRegs; ++r) {
+      if (threadIdx.x + r * 1024 < nv) {
+        const uint16_t* hv = reinterpret_cast<const uint16_t*>(&v[r]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) add(hv[e]);
+      }
+    }
+  } else {
+    for (int c = threadIdx.x; c < S; c += blockDim.x) add(xr[c]);
   }
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   if ((threadIdx.x & 31) == 0) red_s[threadIdx.x >> 5] = s;
