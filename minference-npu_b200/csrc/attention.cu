@@ -6,6 +6,14 @@
 namespace mib200 {
 
 #ifdef MI_TRACE
+// Debug builds only: (clock64, %globaltimer ns) at the first and the last
+// softmax iteration of the traced CTA, for the effective SM clock.
+__device__ unsigned long long g_trace_gt[4];
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 // Debug builds only (-DMI_TRACE): clock64 timeline of the CTA with blockIdx
 // (0,0,0), [event][entry], read back with mi_debug_trace().
 __device__ unsigned long long g_trace[10][4096];
@@ -72,7 +80,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int b = blockIdx.z;
   const int bh = b * p.H + h;
 #ifdef MI_TRACE
-  const bool trace_cta = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 &&
+#ifndef MI_TRACE_HEAD
+#define MI_TRACE_HEAD 0  // head whose heaviest tile is traced
+#endif
+  const bool trace_cta = blockIdx.x == 0 && blockIdx.y == MI_TRACE_HEAD && blockIdx.z == 0 &&
                          (threadIdx.x == 0 || threadIdx.x == 160);
 #endif
 
@@ -291,6 +302,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (j + 1 < n_entries) src.get(j + 1, kb_n, kb1_n, m0_n, m1_n);  // prefetch next entry
 
       MI_TR(0, j);
+#ifdef MI_TRACE
+      if (trace_cta && threadIdx.x == 0 && (j == 0 || j == n_entries - 1)) {
+        g_trace_gt[j == 0 ? 0 : 2] = clock64();
+        g_trace_gt[j == 0 ? 1 : 3] = globaltimer_ns();
+      }
+#endif
       if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, 107)) { ok = false; break; }
       tc_fence_after();
       MI_TR(1, j);
@@ -516,6 +533,12 @@ int launch_attention(const mi_tensor4& q, const mi_tensor4& k, const mi_tensor4&
 }  // namespace mib200
 
 #ifdef MI_TRACE
+extern "C" int mi_debug_trace_gt(unsigned long long* host_out) {
+  return cudaMemcpyFromSymbol(host_out, mib200::g_trace_gt, sizeof(mib200::g_trace_gt)) ==
+                 cudaSuccess
+             ? 0
+             : 4;
+}
 extern "C" int mi_debug_trace(unsigned long long* host_out) {
   return cudaMemcpyFromSymbol(host_out, mib200::g_trace, sizeof(mib200::g_trace)) == cudaSuccess
              ? 0
