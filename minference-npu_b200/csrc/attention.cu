@@ -70,6 +70,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* s_full = v_empty + VS;
   uint64_t* p_full = s_full + 2;
   uint64_t* pv_done = p_full + 2;
+  uint64_t* q_tmem = pv_done + 2;  // the softmax warps staged Q's first KQ dims in TMEM
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlotOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kAbortOff);
 
@@ -130,6 +131,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], kBM);
       mbar_init(&pv_done[i], 1);
+      if (i == 0) mbar_init(q_tmem, kBM);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -233,10 +235,18 @@ __global__ void __launch_bounds__(kThreads, 2)
           const uint32_t koff = (ks & 1) * 32;
           const uint64_t qd = qd0 + (((ks >> 1) * (kBM * 64) + koff) >> 4);
           const uint64_t kdk = kd + (((ks >> 1) * (kBN * 64) + koff) >> 4);
-          umma_f16_ss(tmem_s, qd, kdk, idesc_qk, ks > 0 ? 1u : 0u);
-          if constexpr (SPLIT)  // Q rows [64,128) start 64 rows (4096 B) into each chunk
-            umma_f16_ss(tmem_s + kLane16, qd + ((64 * 64) >> 4), kdk + (L::kKVBytes >> 4),
-                        idesc_qk, ks > 0 ? 1u : 0u);
+          if (ks < L::KQ / 16) {  // A = Q from TMEM (staged by the softmax warps)
+            const uint32_t tq = tmem_base + L::kQCol + ks * 8;
+            umma_f16_ts(tmem_s, tq, kdk, idesc_qk, ks > 0 ? 1u : 0u);
+            if constexpr (SPLIT)
+              umma_f16_ts(tmem_s + kLane16, tq + kLane16, kdk + (L::kKVBytes >> 4), idesc_qk,
+                          ks > 0 ? 1u : 0u);
+          } else {
+            umma_f16_ss(tmem_s, qd, kdk, idesc_qk, ks > 0 ? 1u : 0u);
+            if constexpr (SPLIT)  // Q rows [64,128) start 64 rows (4096 B) into each chunk
+              umma_f16_ss(tmem_s + kLane16, qd + ((64 * 64) >> 4), kdk + (L::kKVBytes >> 4),
+                          idesc_qk, ks > 0 ? 1u : 0u);
+          }
         }
         umma_commit(&s_full[j & 1]);
         umma_commit(&k_empty[st]);
@@ -245,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       MI_TR(5, j);
       return true;
     };
-    bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, 102));
+    bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, 102) && mbar_wait(q_tmem, 0, 111));
     if (ok && n_entries > 0) ok = issue_qk(0);
     for (int j = 0; ok && j < n_entries; ++j) {
       if (*abort_flag) { ok = false; break; }
@@ -291,10 +301,36 @@ __global__ void __launch_bounds__(kThreads, 2)
     float m_used = NEG_INF;
     bool ok = true;
 
+    // Stage this row's first KQ dims of Q in this thread's TMEM lane (the
+    // A operand of the first KQ/16 QK K-steps).  Shared-memory Q is 64-byte
+    // swizzled: 16-byte unit u of row r in chunk c sits at unit u ^ ((r>>1)&3).
+    if (mbar_wait(q_full, 0, 112)) {
+      const uint8_t* qrow = smem + L::kQOff + row * 64;
+      const uint32_t sw = (row >> 1) & 3;
+#pragma unroll
+      for (int c = 0; c < L::KQ / 32; ++c) {
+        uint32_t w[16];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint4 x = *reinterpret_cast<const uint4*>(qrow + c * (kBM * 64) + ((u ^ sw) << 4));
+          w[4 * u + 0] = x.x;
+          w[4 * u + 1] = x.y;
+          w[4 * u + 2] = x.z;
+          w[4 * u + 3] = x.w;
+        }
+        tmem_st16u(lane_base + L::kQCol + c * 16, w);
+      }
+      tmem_wait_st();
+    } else {
+      ok = false;
+    }
+    tc_fence_before();
+    mbar_arrive(q_tmem);
+
     int kb_n = 0, kb1_n = 0;
     uint64_t m0_n = 0, m1_n = 0;
     if (n_entries > 0) src.get(0, kb_n, kb1_n, m0_n, m1_n);
-    for (int j = 0; j < n_entries; ++j) {
+    for (int j = 0; ok && j < n_entries; ++j) {
       const int kb = (row < 64) ? kb_n : kb1_n;  // this row's key block
       const int kb_lo = min(kb_n, kb1_n), kb_hi = max(kb_n, kb1_n);
       const uint64_t mask = (row < 64) ? m0_n : m1_n;

@@ -100,13 +100,23 @@ struct AttnSmem {
   static constexpr int kOCols = D + 16;             // O columns incl. the row-sum column
   // TMEM: S0 [0,64), S1 [64,128), O [128, 128+kOCols); P(j) aliases S(j&1)
   static constexpr uint32_t kTmemCols = (128 + kOCols <= 256) ? 256u : 512u;
+  // The first KQ head dims of the Q tile are also staged in TMEM (columns
+  // [kQCol, kQCol + KQ/2), two 16-bit elements per column): their QK K-steps
+  // read A from TMEM, so they read only K from shared memory.  With both
+  // operands in shared memory an M=128, N=64 MMA step is bound by
+  // shared-memory bandwidth (~48 cycles for 32 cycles of tensor work);
+  // with A in TMEM it runs at the tensor rate.
+  static constexpr int kQCol = 128 + kOCols;
+  static constexpr int KQ = ((int)kTmemCols - kQCol) / 8 * 16 < D
+                                ? ((int)kTmemCols - kQCol) / 8 * 16 : D;
+  static_assert(KQ % 32 == 0, "whole 32-dim chunks of Q in TMEM");
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kQOff + kQBytes;
   static constexpr int kVOff = kKOff + KS * kKStage;
   static constexpr int kBarOff = kVOff + VS * kVStage;
   // barriers: q_full, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
-  //           s_full[2], p_full[2], pv_done[2]
-  static constexpr int kNumBars = 1 + 2 * KS + 2 * VS + 6;
+  //           s_full[2], p_full[2], pv_done[2], q_tmem
+  static constexpr int kNumBars = 1 + 2 * KS + 2 * VS + 7;
   static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
   static constexpr int kAbortOff = kTmemSlotOff + 4;
   static constexpr int kBytes = kAbortOff + 4;
