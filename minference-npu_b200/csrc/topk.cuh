@@ -7,7 +7,9 @@
 //
 // Warp w owns the contiguous index segment [w*seg, (w+1)*seg) and walks it
 // in rounds of 32 consecutive indices, so every load is coalesced and index
-// order inside a round comes from ballots.  Histograms are per warp, and
+// order inside a round comes from ballots.  Rounds are loaded kTopkBatch at a
+// time before they are processed (in order): the keys usually come from L2,
+// and one dependent load per round would serialise on its latency.  Histograms are per warp, and
 // lanes holding the same digit in a round are merged with __match_any_sync
 // into one add: the scores' leading bytes are shared by most keys, so a
 // block-wide histogram would serialise on one or two bins.
@@ -39,6 +41,28 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot, int* t
   __syncthreads();
   *total = tot;
   return base + x - v;
+}
+
+constexpr int kTopkBatch = 8;
+
+// Walks [wbeg, wend) in rounds of 32 indices; f(i, key, valid) is called once
+// per round per lane, rounds in ascending order.
+template <typename F>
+__device__ __forceinline__ void walk_rounds(const uint32_t* keys, int wbeg, int wend, F&& f) {
+  const int lane = threadIdx.x & 31;
+  for (int base = wbeg; base < wend; base += 32 * kTopkBatch) {
+    uint32_t kk[kTopkBatch];
+#pragma unroll
+    for (int u = 0; u < kTopkBatch; ++u) {
+      const int i = base + u * 32 + lane;
+      kk[u] = i < wend ? keys[i] : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < kTopkBatch; ++u) {
+      const int i = base + u * 32 + lane;
+      if (base + u * 32 < wend) f(i, kk[u], i < wend);
+    }
+  }
 }
 
 template <int NT>
@@ -78,13 +102,11 @@ __device__ void block_topk(const uint32_t* keys, int n, int k, TopkSmem<NT>& sm,
 #pragma unroll
     for (int q = 0; q < 8; ++q) sm.hist[warp][lane * 8 + q] = 0;
     __syncwarp();
-    for (int base = wbeg; base < wend; base += 32) {
-      const int i = base + lane;
-      const uint32_t key = i < wend ? keys[i] : 0u;
-      const int d = (i < wend && (key & pmask) == prefix) ? (int)((key >> shift) & 255) : 256;
+    walk_rounds(keys, wbeg, wend, [&](int, uint32_t key, bool valid) {
+      const int d = (valid && (key & pmask) == prefix) ? (int)((key >> shift) & 255) : 256;
       const unsigned same = __match_any_sync(0xffffffffu, d);
       if (d != 256 && lane == __ffs(same) - 1) atomicAdd(&sm.hist[warp][d], __popc(same));
-    }
+    });
     __syncthreads();
     for (int b = tid; b < 256; b += NT) {
       int c = 0;
@@ -134,10 +156,9 @@ __device__ void block_topk(const uint32_t* keys, int n, int k, TopkSmem<NT>& sm,
 
   // Elements equal to T before this warp's segment.
   int eq_w = 0;
-  for (int base = wbeg; base < wend; base += 32) {
-    const int i = base + lane;
-    eq_w += __popc(__ballot_sync(0xffffffffu, i < wend && keys[i] == T));
-  }
+  walk_rounds(keys, wbeg, wend, [&](int, uint32_t key, bool valid) {
+    eq_w += __popc(__ballot_sync(0xffffffffu, valid && key == T));
+  });
   if (lane == 0) sm.warp_cnt[warp] = eq_w;
   __syncthreads();
   const int eq_before = warps_before<NT>(sm.warp_cnt, warp);
@@ -146,10 +167,7 @@ __device__ void block_topk(const uint32_t* keys, int n, int k, TopkSmem<NT>& sm,
   // selected elements) for selected i.  Returns the warp's selected count.
   auto walk = [&](auto&& f) -> int {
     int eq_seen = eq_before, cnt = 0;
-    for (int base = wbeg; base < wend; base += 32) {
-      const int i = base + lane;
-      const bool valid = i < wend;
-      const uint32_t key = valid ? keys[i] : 0u;
+    walk_rounds(keys, wbeg, wend, [&](int i, uint32_t key, bool valid) {
       const bool eq = valid && key == T;
       const unsigned eqb = __ballot_sync(0xffffffffu, eq);
       const bool sel = valid && (key > T || (eq && eq_seen + __popc(eqb & lt) < need_eq));
@@ -157,7 +175,7 @@ __device__ void block_topk(const uint32_t* keys, int n, int k, TopkSmem<NT>& sm,
       if (sel) f(i, cnt + __popc(selb & lt));
       cnt += __popc(selb);
       eq_seen += __popc(eqb);
-    }
+    });
     return cnt;
   };
   const int sel_w = walk([](int, int) {});
