@@ -14,6 +14,8 @@
 // into one add: the scores' leading bytes are shared by most keys, so a
 // block-wide histogram would serialise on one or two bins.
 #pragma once
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace mib200 {
@@ -68,8 +70,10 @@ __device__ __forceinline__ void walk_rounds(const uint32_t* keys, int wbeg, int 
 template <int NT>
 struct TopkSmem {
   int hist[NT / 32][256];  // per-warp digit histograms
-  int tot[256];
+  int tot[256];            // this CTA's histogram
+  int ctot[256];           // the cluster's histogram
   int warp_cnt[NT / 32];
+  int cta_cnt;
   int sel_digit;
   int remaining;
 };
@@ -84,17 +88,44 @@ __device__ __forceinline__ int warps_before(const int* warp_cnt, int w) {
 
 // keys: n entries (shared or global memory).  Calls emit(pos, index) for the
 // k selected indices with pos = 0..k-1 in ascending index order.
-template <int NT, typename Emit>
-__device__ void block_topk(const uint32_t* keys, int n, int k, TopkSmem<NT>& sm, Emit emit) {
+//
+// CL > 1: the calling CTA is one of a cluster of CL CTAs that select
+// together; CTA r owns the index segment [r*cseg, (r+1)*cseg).  Per radix
+// pass each CTA builds its histogram, the cluster sums them through
+// distributed shared memory, and every CTA picks the same digit; the
+// tie-break and output positions use cluster-wide prefix counts.  All CTAs
+// of the cluster must call it with the same arguments.
+template <int NT, int CL, typename Emit>
+__device__ void cluster_topk(const uint32_t* keys, int n, int k, TopkSmem<NT>& sm, Emit emit) {
+  namespace cg = cooperative_groups;
   constexpr int NW = NT / 32;
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
   const unsigned lt = (1u << lane) - 1u;
   if (k <= 0) return;
   if (k > n) k = n;
-  const int seg = (((n + NW - 1) / NW) + 31) & ~31;
-  const int wbeg = min(n, warp * seg);
-  const int wend = min(n, wbeg + seg);
+  int crank = 0;
+  if constexpr (CL > 1) crank = (int)cg::this_cluster().block_rank();
+  auto cluster_sync = [&]() {
+    if constexpr (CL > 1) cg::this_cluster().sync();
+    else __syncthreads();
+  };
+  // Sum over the cluster's CTAs of a shared int (the caller's own included).
+  auto cluster_sum = [&](int* local, int upto_rank) -> int {
+    int s = 0;
+    if constexpr (CL > 1) {
+      for (int r = 0; r < upto_rank; ++r) s += *cg::this_cluster().map_shared_rank(local, r);
+    } else {
+      if (upto_rank > 0) s = *local;
+    }
+    return s;
+  };
+  const int cseg = (((n + CL - 1) / CL) + 31) & ~31;
+  const int cbeg = min(n, crank * cseg);
+  const int cend = min(n, cbeg + cseg);
+  const int seg = ((((cend - cbeg) + NW - 1) / NW) + 31) & ~31;
+  const int wbeg = min(cend, cbeg + warp * seg);
+  const int wend = min(cend, wbeg + seg);
 
   uint32_t prefix = 0, pmask = 0;
   if (tid == 0) sm.remaining = k;
@@ -114,6 +145,8 @@ __device__ void block_topk(const uint32_t* keys, int n, int k, TopkSmem<NT>& sm,
       for (int w = 0; w < NW; ++w) c += sm.hist[w][b];
       sm.tot[b] = c;
     }
+    cluster_sync();  // every CTA's histogram is complete
+    for (int b = tid; b < 256; b += NT) sm.ctot[b] = cluster_sum(&sm.tot[b], CL);
     __syncthreads();
     if (warp == 0) {
       // lane l covers digits [255-8l-7, 255-8l], scanned from the top digit down.
@@ -121,7 +154,7 @@ __device__ void block_topk(const uint32_t* keys, int n, int k, TopkSmem<NT>& sm,
       int s = 0;
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        c[q] = sm.tot[255 - 8 * lane - q];
+        c[q] = sm.ctot[255 - 8 * lane - q];
         s += c[q];
       }
       int incl = s;
@@ -147,24 +180,27 @@ __device__ void block_topk(const uint32_t* keys, int n, int k, TopkSmem<NT>& sm,
         }
       }
     }
-    __syncthreads();
+    cluster_sync();  // no CTA still reads this CTA's tot when the next pass rewrites it
     prefix |= (uint32_t)sm.sel_digit << shift;
     pmask |= 255u << shift;
   }
   const uint32_t T = prefix;
   const int need_eq = sm.remaining;
 
-  // Elements equal to T before this warp's segment.
+  // Elements equal to T before this warp's segment (cluster-wide).
   int eq_w = 0;
   walk_rounds(keys, wbeg, wend, [&](int, uint32_t key, bool valid) {
     eq_w += __popc(__ballot_sync(0xffffffffu, valid && key == T));
   });
   if (lane == 0) sm.warp_cnt[warp] = eq_w;
   __syncthreads();
-  const int eq_before = warps_before<NT>(sm.warp_cnt, warp);
-  __syncthreads();
-  // Walks the segment; calls f(i, rank in the selection among this warp's
-  // selected elements) for selected i.  Returns the warp's selected count.
+  if (tid == 0) sm.cta_cnt = warps_before<NT>(sm.warp_cnt, NW);
+  const int eq_before_warp = warps_before<NT>(sm.warp_cnt, warp);
+  cluster_sync();
+  const int eq_before = eq_before_warp + cluster_sum(&sm.cta_cnt, crank);
+  cluster_sync();
+  // Walks the segment; calls f(i, rank among this warp's selected elements)
+  // for selected i.  Returns the warp's selected count.
   auto walk = [&](auto&& f) -> int {
     int eq_seen = eq_before, cnt = 0;
     walk_rounds(keys, wbeg, wend, [&](int i, uint32_t key, bool valid) {
@@ -181,16 +217,19 @@ __device__ void block_topk(const uint32_t* keys, int n, int k, TopkSmem<NT>& sm,
   const int sel_w = walk([](int, int) {});
   if (lane == 0) sm.warp_cnt[warp] = sel_w;
   __syncthreads();
-  const int pos_base = warps_before<NT>(sm.warp_cnt, warp);
+  if (tid == 0) sm.cta_cnt = warps_before<NT>(sm.warp_cnt, NW);
+  const int pos_warp = warps_before<NT>(sm.warp_cnt, warp);
+  cluster_sync();
+  const int pos_base = pos_warp + cluster_sum(&sm.cta_cnt, crank);
   walk([&](int i, int r) { emit(pos_base + r, i); });
-  __syncthreads();
+  cluster_sync();  // no CTA reads another's shared memory after it exits
 }
 
 // Warp-scope variant: the calling warp selects k of n keys on its own (no
 // block barriers), with `hist` a 256-int scratch private to the warp.  Lane l
 // reads indices l, l+32, ... (conflict-free in shared memory); index order
 // for the tie-break and the output comes from ballots over each group of 32
-// consecutive indices.  Same result as block_topk.
+// consecutive indices.  Same result as cluster_topk.
 template <typename Emit>
 __device__ void warp_topk(const uint32_t* keys, int n, int k, int* hist, Emit emit) {
   const int lane = threadIdx.x & 31;

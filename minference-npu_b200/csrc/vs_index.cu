@@ -281,22 +281,23 @@ __global__ void __launch_bounds__(256) vs_sums_kernel(const uint16_t* x, const f
   skeys[(long long)bh * S + c] = float_to_ordered(ds);
 }
 
-// K3d: the two top-k selections.  Grid (H, B, 2), 1024 threads.
+// K3d: the two top-k selections.  One cluster of kVsSelCluster CTAs per
+// (head, list): grid (H * kVsSelCluster, B, 2), 1024 threads per CTA.
 constexpr int kVsSelThreads = 1024;
-__global__ void __launch_bounds__(kVsSelThreads) vs_select_kernel(const uint32_t* vkeys,
-                                                                  const uint32_t* skeys, int H,
-                                                                  int S, int nv, int ns,
-                                                                  int32_t* v_idx, int32_t* s_idx) {
+constexpr int kVsSelCluster = 8;
+__global__ void __cluster_dims__(kVsSelCluster, 1, 1) __launch_bounds__(kVsSelThreads)
+    vs_select_kernel(const uint32_t* vkeys, const uint32_t* skeys, int H, int S, int nv, int ns,
+                     int32_t* v_idx, int32_t* s_idx) {
   __shared__ TopkSmem<kVsSelThreads> tsm;
-  const int h = blockIdx.x, b = blockIdx.y, bh = b * H + h;
+  const int h = blockIdx.x / kVsSelCluster, b = blockIdx.y, bh = b * H + h;
   if (blockIdx.z == 0) {
     int32_t* dst = v_idx + (long long)bh * nv;
-    block_topk<kVsSelThreads>(vkeys + (long long)bh * S, S, nv, tsm,
-                              [&](int pos, int idx) { dst[pos] = idx; });
+    cluster_topk<kVsSelThreads, kVsSelCluster>(vkeys + (long long)bh * S, S, nv, tsm,
+                                               [&](int pos, int idx) { dst[pos] = idx; });
   } else {
     int32_t* dst = s_idx + (long long)bh * ns;
-    block_topk<kVsSelThreads>(skeys + (long long)bh * S, S, ns, tsm,
-                              [&](int pos, int idx) { dst[pos] = S - 1 - idx; });
+    cluster_topk<kVsSelThreads, kVsSelCluster>(skeys + (long long)bh * S, S, ns, tsm,
+                                               [&](int pos, int idx) { dst[pos] = S - 1 - idx; });
   }
 }
 
@@ -515,7 +516,7 @@ extern "C" int mi_vs_estimate(mi_tensor4 q, mi_tensor4 k, int64_t B, int64_t H, 
     vs_rowstats_kernel<__half><<<g2, 1024, 0, st>>>(x, (int)H, (int)S, LQ, stats);
     vs_sums_kernel<__half><<<g3, 256, 0, st>>>(x, stats, (int)H, (int)S, LQ, vkeys, skeys);
   }
-  dim3 g4((unsigned)H, (unsigned)B, 2);
+  dim3 g4((unsigned)(H * kVsSelCluster), (unsigned)B, 2);
   vs_select_kernel<<<g4, kVsSelThreads, 0, st>>>(vkeys, skeys, (int)H, (int)S, (int)vertical_size,
                                                  (int)slash_size, v_idx, s_idx);
   return cudaGetLastError() == cudaSuccess ? MI_OK : MI_ERR_LAUNCH;
