@@ -303,7 +303,8 @@ __global__ void __cluster_dims__(kVsSelCluster, 1, 1) __launch_bounds__(kVsSelTh
 
 // ---------------------------------------------------------------------------
 // K4a: per-head tables for the direct mask.
-//   P[x]      number of distinct slashes s < x (x = 0..S)
+//   slashes   bitset of the selected slashes with per-word prefix counts
+//             (SlashSet below; stored in the head's (S+1)-int P region)
 //   vmask[kb] vertical columns of key block kb (64-bit)
 //   smask[D]  for query block bq and key block kb = bq - D (not the ragged
 //             last query block): key 64*kb + c is covered by a slash iff some
@@ -311,11 +312,27 @@ __global__ void __cluster_dims__(kVsSelCluster, 1, 1) __launch_bounds__(kVsSelTh
 //   clow[bq]  some slash s in (64*bq, 64*bq + 64) (range clamped to [0,64))
 // Grid (H, B), 1024 threads.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ bool any_slash(const int* P, long long lo, long long hi, int S) {
+// The selected slashes of a head as a bitset over [0, S) plus, per 32-bit
+// word, the number of set bits in the words before it (nwords + 1 entries):
+// the count of slashes in any range is two lookups and two popcounts.
+struct SlashSet {
+  const uint32_t* bits;
+  const int* wpre;
+};
+
+__device__ __forceinline__ int vs_slash_words(int S) { return (S + 31) >> 5; }
+
+// Number of selected slashes s < x, for 0 <= x <= S.
+__device__ __forceinline__ int slash_rank(const SlashSet& ss, long long x) {
+  const int w = (int)(x >> 5), r = (int)(x & 31);
+  return ss.wpre[w] + (r ? __popc(ss.bits[w] & ((1u << r) - 1u)) : 0);
+}
+
+__device__ __forceinline__ bool any_slash(const SlashSet& ss, long long lo, long long hi, int S) {
   if (lo < 0) lo = 0;
   if (hi > S - 1) hi = S - 1;
   if (hi < lo) return false;
-  return P[hi + 1] - P[lo] > 0;
+  return slash_rank(ss, hi + 1) - slash_rank(ss, lo) > 0;
 }
 
 __global__ void __launch_bounds__(1024) vs_tables_kernel(const int32_t* v_idx, int nv,
@@ -325,16 +342,18 @@ __global__ void __launch_bounds__(1024) vs_tables_kernel(const int32_t* v_idx, i
                                                          uint32_t* smask_all, int* clow_all) {
   __shared__ int warp_tot[32];
   const int h = blockIdx.x, b = blockIdx.y, bh = b * H + h;
-  int* P = Pall + (long long)bh * (S + 1);
+  const int nw = vs_slash_words(S);
+  uint32_t* bits = reinterpret_cast<uint32_t*>(Pall + (long long)bh * (S + 1));
+  int* wpre = reinterpret_cast<int*>(bits + nw);
   unsigned long long* vmask = vmask_all + (long long)bh * nb;
   uint32_t* smask = smask_all + (long long)bh * nb * 2;
   int* clow = clow_all + (long long)bh * nb;
-  for (int i = threadIdx.x; i <= S; i += blockDim.x) P[i] = 0;
+  for (int i = threadIdx.x; i < nw; i += blockDim.x) bits[i] = 0u;
   for (int i = threadIdx.x; i < nb; i += blockDim.x) vmask[i] = 0ull;
   __syncthreads();
   for (int i = threadIdx.x; i < ns; i += blockDim.x) {
-    const int s = s_idx[(long long)bh * ns + i];
-    if (s >= 0 && s < S) P[s] = 1;
+    const int sl = s_idx[(long long)bh * ns + i];
+    if (sl >= 0 && sl < S) atomicOr(&bits[sl >> 5], 1u << (sl & 31));
   }
   for (int i = threadIdx.x; i < nv; i += blockDim.x) {
     int c = v_idx[(long long)bh * nv + i];
@@ -342,39 +361,36 @@ __global__ void __launch_bounds__(1024) vs_tables_kernel(const int32_t* v_idx, i
     atomicOr(&vmask[c >> 6], 1ull << (c & 63));
   }
   __syncthreads();
-  // exclusive scan of P[0..S] in place
-  const int n = S + 1;
-  const int ept = (n + blockDim.x - 1) / blockDim.x;
-  const int beg = min(n, (int)threadIdx.x * ept), end = min(n, beg + ept);
+  // wpre: exclusive prefix of the word popcounts (contiguous word chunks per thread)
+  const int ept = (nw + blockDim.x - 1) / blockDim.x;
+  const int beg = min(nw, (int)threadIdx.x * ept), end = min(nw, beg + ept);
   int local = 0;
-  for (int i = beg; i < end; ++i) local += P[i];
+  for (int i = beg; i < end; ++i) local += __popc(bits[i]);
   int tot;
-  const int pre = block_exclusive_scan<1024>(local, warp_tot, &tot);
-  int run = pre;
+  int run = block_exclusive_scan<1024>(local, warp_tot, &tot);
   for (int i = beg; i < end; ++i) {
-    const int vv = P[i];
-    P[i] = run;
-    run += vv;
+    wpre[i] = run;
+    run += __popc(bits[i]);
   }
+  if (threadIdx.x == 0) wpre[nw] = tot;
   __syncthreads();
+  const SlashSet ss{bits, wpre};
   for (int base = 0; base < nb * 64; base += blockDim.x) {
     const int idx = base + threadIdx.x;
     bool bit = false;
     if (idx < nb * 64) {
       const long long Dl = idx >> 6, c = idx & 63;
       const long long d = Dl * 64 - c;
-      bit = any_slash(P, d, d + 63, S);
+      bit = any_slash(ss, d, d + 63, S);
     }
     const unsigned bal = __ballot_sync(0xffffffffu, bit);
     if ((threadIdx.x & 31) == 0 && idx < nb * 64) smask[idx >> 5] = bal;
   }
   for (int bq = threadIdx.x; bq < nb; bq += blockDim.x)
-    clow[bq] = any_slash(P, (long long)bq * 64 + 1, (long long)bq * 64 + 63, S) ? 1 : 0;
+    clow[bq] = any_slash(ss, (long long)bq * 64 + 1, (long long)bq * 64 + 63, S) ? 1 : 0;
 }
 
-// Mask of key block kb for query block bq (rows [64bq, 64bq+64)), before the
-// per-element causal / key < S test applied by the attention kernel.
-__device__ __forceinline__ uint64_t vs_block_mask(int bq, int kb, int S, int nb, const int* P,
+__device__ __forceinline__ uint64_t vs_block_mask(int bq, int kb, int S, int nb, const SlashSet& P,
                                                   const unsigned long long* vmask,
                                                   const uint32_t* smask, const int* clow) {
   uint64_t m = vmask[kb];
@@ -412,7 +428,8 @@ __global__ void __launch_bounds__(128) vs_plan_kernel(int H, int S, int nb, int 
   const int t = blockIdx.x * 4 + w;
   const int h = blockIdx.y, b = blockIdx.z, bh = b * H + h;
   if (t >= T) return;
-  const int* P = Pall + (long long)bh * (S + 1);
+  const uint32_t* pb = reinterpret_cast<const uint32_t*>(Pall + (long long)bh * (S + 1));
+  const SlashSet P{pb, reinterpret_cast<const int*>(pb + vs_slash_words(S))};
   const unsigned long long* vmask = vmask_all + (long long)bh * nb;
   const uint32_t* smask = smask_all + (long long)bh * nb * 2;
   const int* clow = clow_all + (long long)bh * nb;
