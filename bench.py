@@ -160,7 +160,7 @@ def vs_visible_pairs(v_idx: torch.Tensor, s_idx: torch.Tensor, S: int) -> int:
 # clocks sampler (nvidia-smi during the timed region)
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -182,11 +182,23 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append((time.monotonic(), line.strip()))
+            self.lines.append(line.strip())
+
+    @staticmethod
+    def _sample_time(ts: str) -> float | None:
+        """Epoch seconds of an nvidia-smi timestamp ("YYYY/MM/DD HH:MM:SS.mmm",
+        local time).  The sample's own time, not when the line was read: the
+        pipe delivers nvidia-smi's output in bursts."""
+        import datetime
+
+        try:
+            return datetime.datetime.strptime(ts.strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            return None
 
     def stop(self, t_lo: float | None = None, t_hi: float | None = None) -> dict:
-        """Summary of the samples taken between host times t_lo and t_hi (the
-        timed region; all samples if not given)."""
+        """Summary of the samples taken between wall-clock times t_lo and t_hi
+        (time.time(); the timed region; all samples if not given)."""
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -196,12 +208,15 @@ class ClockSampler:
             self.proc.kill()
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ts, ln in self.lines:
-            if (t_lo is not None and ts < t_lo) or (t_hi is not None and ts > t_hi):
-                continue
+        for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
+            ts = self._sample_time(parts[0])
+            if ts is not None and ((t_lo is not None and ts < t_lo) or
+                                   (t_hi is not None and ts > t_hi)):
+                continue
+            parts = parts[1:]
             try:
                 sm.append(float(parts[1]))
                 smax = float(parts[2])
@@ -715,13 +730,13 @@ def main():
     evs: list = []
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    t_lo = time.monotonic()
+    t_lo = time.time()
     t0.record()
     for _ in range(args.steps):
         step(ev=evs)
     t1.record()
     barrier()
-    t_hi = time.monotonic()
+    t_hi = time.time()
     clk = clocks.stop(t_lo, t_hi)  # samples inside the timed region only
     ms = t0.elapsed_time(t1) / args.steps
     ms = max_over_ranks(ms)
