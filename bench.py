@@ -235,7 +235,8 @@ class ClockSampler:
 class Layer:
     """One rank's share of the layer: inputs resident on the device."""
 
-    def __init__(self, rank, world, S, device, pattern="mixed", n_heads=H_TOTAL, head_map=None):
+    def __init__(self, rank, world, S, device, pattern="mixed", n_heads=H_TOTAL, head_map=None,
+                 head_major_out=False):
         from minference import ops
 
         self.ops = ops
@@ -244,9 +245,16 @@ class Layer:
         self.groups = shard_groups(rank, world, pattern, n_heads, head_map)
         self.heads = [h for _, hs in self.groups for h in hs]
         self.q, self.k, self.v = make_inputs(self.heads, S, device)
-        # output stored [B, S, H_rank, D] (what o_proj consumes), written through a BNSD view
-        self.out_bshd = torch.empty(1, S, len(self.heads), D, dtype=torch.bfloat16, device=device)
-        self.out = self.out_bshd.transpose(1, 2)
+        # output stored [B, S, H_rank, D] (what o_proj consumes), written through a BNSD view;
+        # head_major_out: stored [B, H_rank, S, D] instead (each head contiguous, so a
+        # range of heads can be all-gathered while later heads are still computed)
+        if head_major_out:
+            self.out = torch.empty(1, len(self.heads), S, D, dtype=torch.bfloat16, device=device)
+            self.out_bshd = self.out
+        else:
+            self.out_bshd = torch.empty(1, S, len(self.heads), D, dtype=torch.bfloat16,
+                                        device=device)
+            self.out = self.out_bshd.transpose(1, 2)
         self.slices = []
         h0 = 0
         for p, hs in self.groups:
@@ -255,9 +263,11 @@ class Layer:
         # the same groups as (pattern key, local heads), the dispatcher's format
         self.run_spec = [(PATTERN_KEYS[p], list(range(sl.start, sl.stop))) for p, sl in self.slices]
 
-    def run(self, q=None, k=None, v=None, ev=None):
+    def run(self, q=None, k=None, v=None, ev=None, after_group=None):
         """One step.  ev: optional list collecting (start, end) events of the
-        attention phase of each group (index estimation excluded)."""
+        attention phase of each group (index estimation excluded).
+        after_group(heads_done): called after each group's launches are queued,
+        with the number of local heads (in output order) complete by then."""
         ops = self.ops
         q = self.q if q is None else q
         k = self.k if k is None else k
@@ -282,6 +292,8 @@ class Layer:
                 b = torch.cuda.Event(enable_timing=True)
                 b.record()
                 ev.append((a, b))
+            if after_group is not None:
+                after_group(sl.stop)
         return self.out_bshd
 
     @staticmethod
@@ -671,12 +683,23 @@ def main():
 
     S = args.seq
     head_map = head_map_for(world, args.pattern, args.heads, args.head_map, S)
-    layer = Layer(rank, world, S, device, args.pattern, args.heads, head_map)
+    # N>1, attention only: the layer output is all-gathered in two halves (by
+    # local head), the first half as soon as its heads are done, overlapping
+    # the attention of the rest.
+    split_gather = world > 1 and args.o_proj == "none"
+    layer = Layer(rank, world, S, device, args.pattern, args.heads, head_map,
+                  head_major_out=split_gather)
     n_heads = args.heads
     gathered = None
-    if world > 1:
+    if world > 1 and not split_gather:
         gathered = torch.empty((world,) + tuple(layer.out_bshd.shape), dtype=torch.bfloat16,
                                device=device)
+    if split_gather:
+        h_loc = len(layer.heads)
+        half = h_loc // 2
+        gbufs = [torch.empty((world, 1, n, S, D), dtype=torch.bfloat16, device=device)
+                 for n in (half, h_loc - half)]
+        comm_stream = torch.cuda.Stream(device=device)
 
     w_oproj = None
     if world > 1 and args.o_proj != "none":
@@ -687,6 +710,26 @@ def main():
         w_oproj = w.to(torch.bfloat16)[:, o_proj_input_permutation(head_map, D).to(device)]
 
     def step(q=None, k=None, v=None, ev=None):
+        if split_gather:
+            sent = []
+
+            def after_group(done):
+                if not sent and done >= half and half > 0:
+                    # heads [0, half) are complete on this rank once the work
+                    # queued so far has run: gather them on the side stream
+                    e = torch.cuda.Event()
+                    e.record()
+                    comm_stream.wait_event(e)
+                    with torch.cuda.stream(comm_stream):
+                        torch.distributed.all_gather_into_tensor(gbufs[0], layer.out[:, :half])
+                    sent.append(True)
+
+            o = layer.run(q, k, v, ev, after_group)
+            if not sent and half > 0:
+                after_group(half)
+            torch.distributed.all_gather_into_tensor(gbufs[1], layer.out[:, half:])
+            torch.cuda.current_stream(device).wait_stream(comm_stream)
+            return o
         o = layer.run(q, k, v, ev)
         if world > 1:
             if args.o_proj == "overlap":
@@ -823,6 +866,9 @@ def main():
                        "model": "Phi-3-mini-128k attention shape", "global_batch": 1, "seq_len": S,
                        "heads": n_heads, "head_dim": D, "pattern": args.pattern,
                        "parallelism": f"head-shard{world}" if world > 1 else "single",
+                       "gather": ("all-gather in two halves by local head, the first overlapped "
+                                  "with the remaining attention" if split_gather else
+                                  ("one all-gather" if world > 1 else "none")),
                        "head_map": args.head_map if world > 1 else "single",
                        "o_proj": args.o_proj if world > 1 else "none",
                        "l2": "inputs 1.2 GB > L2 (no flush needed)"},
