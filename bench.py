@@ -75,7 +75,9 @@ def shard_groups(rank: int, world: int, pattern: str = "mixed", n_heads: int = H
     heads = head_map[rank] if head_map is not None else list(range(rank * per, (rank + 1) * per))
     pats = head_patterns(n_heads) if pattern == "mixed" else [pattern] * n_heads
     groups = []
-    for p in ("vertical_and_slash", "block_sparse", "stream_llm", "dense"):
+    # cheapest groups first: with N>1 the first half of the heads (the first
+    # all-gather) is then ready early and its transfer hides behind the rest
+    for p in ("stream_llm", "block_sparse", "vertical_and_slash", "dense"):
         hs = [h for h in heads if pats[h] == p]
         if hs:
             groups.append((p, hs))
