@@ -8,7 +8,7 @@ namespace mib200 {
 #ifdef MI_TRACE
 // Debug builds only: (clock64, %globaltimer ns) at the first and the last
 // softmax iteration of the traced CTA, for the effective SM clock.
-__device__ unsigned long long g_trace_gt[4];
+__device__ unsigned long long g_trace_gt[8];  // [4..7]: kernel entry, setup done, loop done, exit
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -86,6 +86,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #endif
   const bool trace_cta = blockIdx.x == 0 && blockIdx.y == MI_TRACE_HEAD && blockIdx.z == 0 &&
                          (threadIdx.x == 0 || threadIdx.x == 160);
+  if (trace_cta && threadIdx.x == 0) g_trace_gt[4] = clock64();
 #endif
 
   // ---- entry list of this tile -------------------------------------------
@@ -154,6 +155,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+#ifdef MI_TRACE
+  if (trace_cta && threadIdx.x == 0) g_trace_gt[5] = clock64();
+#endif
 
   if (warp == 4) {
     // ======================= TMA producer (one thread) =========================
@@ -453,6 +457,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       MI_TR(4, j);
     }
 
+#ifdef MI_TRACE
+    if (trace_cta && threadIdx.x == 0) g_trace_gt[6] = clock64();
+#endif
     // ---- epilogue: O / l -> shared (Q tile area, swizzled) -> TMA store -----
     if (!ok) *abort_flag = 1;
     bool have_o = false;
@@ -509,6 +516,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     tc_fence_after();
     tmem_dealloc(tmem_base, L::kTmemCols);
   }
+#ifdef MI_TRACE
+  if (trace_cta && threadIdx.x == 0) g_trace_gt[7] = clock64();
+#endif
 }
 
 // ---------------------------------------------------------------------------
