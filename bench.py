@@ -369,11 +369,21 @@ def cpu_reference_sample(S: int, budget_s: float = 12.0) -> dict:
     timed on a bounded sample of query rows and extrapolated to the layer."""
     from oracle import oracle as O
 
-    threads = torch.get_num_threads()
+    # All the host cores this process may use, for numpy's BLAS (the masked
+    # attention's matmuls) and torch: launchers such as torchrun set
+    # OMP_NUM_THREADS=1, which would time a single-threaded CPU.
+    ncores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    torch.set_num_threads(ncores)
     try:
-        import threadpoolctl  # noqa: F401
+        from threadpoolctl import threadpool_info, threadpool_limits
+
+        limiter = threadpool_limits(limits=ncores)
+        blas = [d.get("num_threads", 1) for d in threadpool_info()
+                if d.get("user_api") == "blas"]
+        threads = max(blas) if blas else torch.get_num_threads()
     except Exception:  # noqa: BLE001
-        pass
+        limiter = None
+        threads = torch.get_num_threads()
     rng = np.random.default_rng(0)
     pats = head_patterns()
     rows_total = 0
@@ -403,6 +413,8 @@ def cpu_reference_sample(S: int, budget_s: float = 12.0) -> dict:
                 break
     per_row = t_total / max(rows_total, 1)
     layer_s = per_row * S * H_TOTAL
+    if limiter is not None:
+        limiter.restore_original_limits()
     return {"layer_s": layer_s, "cores": threads, "rows": rows_total, "seconds": t_total}
 
 
