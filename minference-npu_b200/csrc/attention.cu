@@ -23,11 +23,6 @@ __device__ unsigned long long g_trace[10][4096];
 #define MI_TR(ev, j) do { } while (0)
 #endif
 
-// MI_POLY_FULL (default 0; measured neutral): in fully visible blocks one exp2 pair in four runs on
-// the FMA pipe (poly_exp2x2) instead of MUFU.
-#ifndef MI_POLY_FULL
-#define MI_POLY_FULL 0
-#endif
 
 // Softmax of one 64-key block for one query row, in registers.
 // s: raw scores (overwritten).  Returns the block max of raw visible scores.
@@ -372,7 +367,6 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t tmem_s = lane_base + (j & 1) * kBN;
 
       float s[kBN];
-      float tmax = NEG_INF;
       if (!all_empty) {
         tmem_ld32(tmem_s, *reinterpret_cast<float(*)[32]>(&s[0]));
         tmem_ld32(tmem_s + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
@@ -381,6 +375,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
           for (int c = 0; c < kBN; ++c) s[c] = ((vis >> c) & 1ull) ? s[c] : NEG_INF;
         }
+      }
+      auto row_max = [&]() -> float {
         float mx0 = fmax3(s[0], s[1], s[2]);
         float mx1 = fmax3(s[3], s[4], s[5]);
         float mx2 = fmax3(s[6], s[7], s[8]);
@@ -392,11 +388,36 @@ __global__ void __launch_bounds__(kThreads, 2)
           mx2 = fmax3(mx2, s[c + 4], s[c + 5]);
           mx3 = fmax3(mx3, s[c + 6], s[c + 7]);
         }
-        tmax = fmaxf(fmax3(mx0, mx1, fmax3(s[60], s[61], s[62])), fmax3(mx2, mx3, s[63]));
+        return fmaxf(fmax3(mx0, mx1, fmax3(s[60], s[61], s[62])), fmax3(mx2, mx3, s[63]));
+      };
+      // P = 2^(s*scale_log2 - m_used), packed in pairs.
+      uint32_t pk[kBN / 2];
+      auto exp_block = [&](float nm) {
+#pragma unroll
+        for (int c = 0; c < kBN / 2; ++c) {
+          const float x0 = __fmaf_rn(s[2 * c], sc, nm);
+          const float x1 = __fmaf_rn(s[2 * c + 1], sc, nm);
+          pk[c] = DType<DT>::pack2(fast_exp2(x0), fast_exp2(x1));
+        }
+      };
+      // With the lazy rescale, P is relative to the running max m_used, which
+      // rarely moves after the first blocks.  So P is computed against m_used
+      // straight away, with the block max taken alongside (ALU work that
+      // overlaps the MUFU exp2) instead of before it; only if some row's max
+      // grew past the threshold does the warp rescale O and recompute P.  The
+      // result is the same as computing the max first.
+      const bool spec = j > 0 && !all_empty && __all_sync(0xffffffffu, m_used != NEG_INF);
+      float tmax = NEG_INF;
+      if (spec) {
+        exp_block(-m_used);
+        tmax = row_max();
+      } else if (!all_empty) {
+        tmax = row_max();
       }
       MI_TR(2, j);
       const float m_new = fmaxf(m_used, tmax * sc);
       const bool need = m_new > m_used + 8.0f;
+      bool fresh = !spec;  // P still to be computed (or recomputed)
       if (j == 0) {
         m_used = m_new;
       } else if (__any_sync(0xffffffffu, need)) {
@@ -415,37 +436,16 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         tmem_wait_st();
         if (need) m_used = m_new;
+        fresh = true;
       }
-      // P = 2^(s*scale_log2 - m_used); rows with nothing visible yet keep P = 0.
-      // The row sums of P come out of the PV MMA (column D of O).
-      uint32_t pk[kBN / 2];
-      if (all_empty || m_used == NEG_INF) {
+      // Rows with nothing visible yet keep P = 0.  The row sums of P come out
+      // of the PV MMA (column D of O).
+      if (fresh) {
+        if (all_empty || m_used == NEG_INF) {
 #pragma unroll
-        for (int c = 0; c < kBN / 2; ++c) pk[c] = 0u;
-      } else {
-        const float nm = -m_used;
-        if (all_full) {
-          // Fully visible block: one pair in four is exponentiated on the FMA pipe
-          // (poly_exp2x2), the rest on MUFU, which is the softmax's throughput limit.
-#pragma unroll
-          for (int c = 0; c < kBN / 2; ++c) {
-            const float x0 = __fmaf_rn(s[2 * c], sc, nm);
-            const float x1 = __fmaf_rn(s[2 * c + 1], sc, nm);
-            if (MI_POLY_FULL && (c & 3) == 3) {
-              float p0, p1;
-              poly_exp2x2(pk2(fmaxf(x0, -127.f), fmaxf(x1, -127.f)), p0, p1);
-              pk[c] = DType<DT>::pack2(p0, p1);
-            } else {
-              pk[c] = DType<DT>::pack2(fast_exp2(x0), fast_exp2(x1));
-            }
-          }
+          for (int c = 0; c < kBN / 2; ++c) pk[c] = 0u;
         } else {
-#pragma unroll
-          for (int c = 0; c < kBN / 2; ++c) {
-            const float x0 = __fmaf_rn(s[2 * c], sc, nm);
-            const float x1 = __fmaf_rn(s[2 * c + 1], sc, nm);
-            pk[c] = DType<DT>::pack2(fast_exp2(x0), fast_exp2(x1));
-          }
+          exp_block(-m_used);
         }
       }
       MI_TR(3, j);
