@@ -71,6 +71,10 @@ def layer_attention_from_host(q_host: torch.Tensor, k_host: torch.Tensor, v_host
     copy_in, copy_out = _side_streams(dev)
     main = torch.cuda.current_stream(dev)
 
+    # Expensive groups first: a chunk's attention then overlaps the transfers
+    # of the cheaper chunks behind it, and the pipeline ends on short work.
+    cost = {"vertical_and_slash": 0, "dense": 0, "block_sparse": 1, "stream_llm": 2}
+    groups = sorted(groups, key=lambda g: cost.get(g[0][0], 3))
     chunks = []
     for gkey, heads in groups:
         heads = list(heads)
