@@ -5,6 +5,13 @@
 
 namespace mib200 {
 
+// Lazy rescale: O and P stay relative to a running max m_used until a row's
+// max exceeds it by more than 2^MI_RESCALE_LOG2 (P then stays below that
+// power of two: representable in fp16 and bf16).
+#ifndef MI_RESCALE_LOG2
+#define MI_RESCALE_LOG2 12.0f
+#endif
+
 #ifdef MI_TRACE
 // Debug builds only: (clock64, %globaltimer ns) at the first and the last
 // softmax iteration of the traced CTA, for the effective SM clock.
@@ -416,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       MI_TR(2, j);
       const float m_new = fmaxf(m_used, tmax * sc);
-      const bool need = m_new > m_used + 8.0f;
+      const bool need = m_new > m_used + MI_RESCALE_LOG2;
       bool fresh = !spec;  // P still to be computed (or recomputed)
       if (j == 0) {
         m_used = m_new;
