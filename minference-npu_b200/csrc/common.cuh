@@ -223,20 +223,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
       : "r"(taddr));
 }
 
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
-  const uint32_t* r = reinterpret_cast<const uint32_t*>(v);
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32"
-      " [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
-      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
-      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
-      "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
-}
-
 // 32 lanes x 32 bit, 16 consecutive columns.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   uint32_t* r = reinterpret_cast<uint32_t*>(v);
@@ -300,76 +286,6 @@ __device__ __forceinline__ void bulk_wait_read0() {
 }
 __device__ __forceinline__ void named_barrier(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
-
-// Non-blocking probe of an mbarrier phase (used by the producer's event loop).
-__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// 2^x on the FMA/ALU pipes (no MUFU): round-to-nearest split x = j + f,
-// f in [-0.5, 0.5], 2^f by a degree-3 polynomial fitted here for minimum
-// relative error on that interval (max rel. error 7.5e-5, far below the
-// bf16/fp16 rounding P receives), then j added to the exponent field.
-// Valid for x in [-127, 127]; callers clamp.
-__device__ __forceinline__ float poly_exp2(float x) {
-  const float kRound = 12582912.0f;  // 1.5 * 2^23: float add rounds to an integer
-  const float t = __fadd_rn(x, kRound);
-  const float j = __fsub_rn(t, kRound);
-  const float f = __fsub_rn(x, j);
-  float p = __fmaf_rn(0.05517166f, f, 0.24261114f);
-  p = __fmaf_rn(p, f, 0.69326097f);
-  p = __fmaf_rn(p, f, 0.99992806f);
-  const int ji = __float_as_int(t) - 0x4B400000;
-  return __int_as_float(__float_as_int(p) + (int)((unsigned)ji << 23));
-}
-
-// Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction per pair).
-__device__ __forceinline__ uint64_t pk2(float a, float b) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ void upk2(uint64_t v, float& a, float& b) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
-}
-__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
-__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-
-// poly_exp2 on a pair, with the FMA-pipe steps done as f32x2 operations.
-__device__ __forceinline__ void poly_exp2x2(uint64_t x2, float& r0, float& r1) {
-  const uint64_t kRound2 = pk2(12582912.0f, 12582912.0f);
-  const uint64_t kNegRound2 = pk2(-12582912.0f, -12582912.0f);
-  const uint64_t kNegOne2 = pk2(-1.0f, -1.0f);
-  const uint64_t t = fadd2(x2, kRound2);
-  const uint64_t j = fadd2(t, kNegRound2);
-  const uint64_t f = ffma2(j, kNegOne2, x2);
-  uint64_t p = ffma2(pk2(0.05517166f, 0.05517166f), f, pk2(0.24261114f, 0.24261114f));
-  p = ffma2(p, f, pk2(0.69326097f, 0.69326097f));
-  p = ffma2(p, f, pk2(0.99992806f, 0.99992806f));
-  float t0, t1, p0, p1;
-  upk2(t, t0, t1);
-  upk2(p, p0, p1);
-  const int j0 = __float_as_int(t0) - 0x4B400000;
-  const int j1 = __float_as_int(t1) - 0x4B400000;
-  r0 = __int_as_float(__float_as_int(p0) + (int)((unsigned)j0 << 23));
-  r1 = __int_as_float(__float_as_int(p1) + (int)((unsigned)j1 << 23));
 }
 
 // Mask with bits [0, n) set; n clamped to [0, 64].
