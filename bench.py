@@ -333,7 +333,8 @@ class Layer:
 
 
 # DRAM read + write bytes per head of one attention launch at S = 65536, D = 96,
-# bf16, from one ncu capture (profiles/attn_dram_traffic_64k.md).
+# bf16: dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of a
+# 5-head layer (2 vertical_and_slash, 2 block_sparse, 1 stream_llm heads).
 ATTN_DRAM_BYTES_PER_HEAD_64K = {"vertical_and_slash": 49.4e6, "block_sparse": 42.2e6,
                                 "stream_llm": 37.9e6}
 
@@ -894,7 +895,7 @@ def main():
                          "unit": "TFLOP/s", "frac": achieved / tf_peak,
                          "traffic": attn_traffic_bytes(layer, S),
                          "traffic_note": "DRAM read+write bytes per step of the attention launches: "
-                                         "ncu per-head figures (profiles/attn_dram_traffic_64k.md) "
+                                         "ncu per-head figures of a 5-head capture "
                                          "times this rank's heads per pattern; null off S=65536",
                          "peak_kind": peak_kind,
                          "kernel": "attn_fwd_kernel (+ plan kernels), visible-pair FLOPs 4*D*N_vis",
