@@ -1,9 +1,9 @@
 """Generate golden vectors from the reference implementation itself.
 
-Run in a container that has the reference checkout (default
-/root/reference/MInference-NPU, override with MINFERENCE_REF):
+Run where the reference checkout exists, with MINFERENCE_REF set to its
+MInference-NPU directory:
 
-    python tests/golden/make_golden.py
+    MINFERENCE_REF=<path to MInference-NPU> python tests/golden/make_golden.py
 
 It imports the reference's own CPU code paths (the NPU paths are not
 importable without torch_npu) and stores seeded inputs together with the
@@ -35,10 +35,12 @@ import torch.nn.functional as F
 
 sys.dont_write_bytecode = True
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("MINFERENCE_REF", "/root/reference/MInference-NPU")
+REF = os.environ.get("MINFERENCE_REF", "")
 
 
 def _load_ref_package():
+    if not REF or not os.path.isdir(os.path.join(REF, "minference")):
+        raise SystemExit("set MINFERENCE_REF to the reference's MInference-NPU directory")
     pkg_dir = os.path.join(REF, "minference")
     spec = importlib.util.spec_from_file_location(
         "ref_minference", os.path.join(pkg_dir, "__init__.py"), submodule_search_locations=[pkg_dir]
