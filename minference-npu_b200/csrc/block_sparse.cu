@@ -137,6 +137,9 @@ __global__ void __launch_bounds__(kSelThreads) block_select_kernel(
 #pragma unroll
     for (int r = 0; r < kSelRows; ++r) acc[r] = 0.f;
     if (kb <= last_bq) {
+      // Unrolled so that several pooled-K loads (L2) are in flight ahead of
+      // their fmaf steps; each row's chain still runs over d in order.
+#pragma unroll 8
       for (int d = 0; d < D; ++d) {
         const float kv = kp[(long long)d * nbk + kb];
 #pragma unroll
