@@ -615,7 +615,7 @@ def run_ttft(args) -> None:
             model = Phi3ForCausalLM(phi3_mini_config()).eval()
         torch.set_default_dtype(prev)
         if attn_type != "hf":
-            model = MInference(attn_type, model_name="microsoft/Phi-3-mini-128k-instruct")(model)
+            model = MInference(attn_type, model_name=args.model_name)(model)
         for ctx in ctxs:
             g = torch.Generator(device=device).manual_seed(ctx)
             ids = torch.randint(0, 32064, (1, ctx), generator=g, device=device)
@@ -657,6 +657,9 @@ def main():
     ap.add_argument("--ctx", default="4096,8192,16384,32768,65536")
     ap.add_argument("--attn-types", default="minference,dense,hf")
     ap.add_argument("--ttft-runs", type=int, default=2)
+    ap.add_argument("--model-name", default="minference-b200/Phi-3-mini-128k-seeded-mixed",
+                    help="registered pattern config for --ttft (microsoft/Phi-3-mini-128k-instruct "
+                         "is the reference's own 981-dense + 43-stream_llm config)")
     ap.add_argument("--o-proj", default="none", choices=["none", "serial", "overlap"],
                     help="N>1: follow the all-gather with Phi-3's o_proj GEMM, either after "
                          "the whole gather (serial) or chunk by chunk behind it (overlap)")

@@ -14,6 +14,8 @@
  *   mi_stream_fwd         minference/ops/streaming_kernel_npu.py:349-397
  *                         (streaming_forward; band FA + sink FA + LSE merge
  *                          at :233-341 become one kernel)
+ *   mi_dense_fwd          minference/backend_npu/attention.py:192-293
+ *                         (dense_attention, prefill_dense, decode_dense)
  *   mi_block_pool_topk    minference/ops/block_sparse_kernel_npu.py:230-263
  *                         (_select_block_sparse_topk_indices)
  *   mi_block_sparse_fwd   minference/ops/block_sparse_kernel_npu.py:452-601
@@ -73,6 +75,16 @@ int mi_get_device_error(int* code);
 int mi_stream_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor4 out, int64_t B,
                   int64_t H, int64_t S_q, int64_t S_k, int64_t D, int dtype, int64_t n_init,
                   int64_t n_local, float softmax_scale, void* stream);
+
+/* Dense attention, causal (bottom-right aligned when S_q < S_k: row r sees
+ * keys j <= S_k - S_q + r) or not causal (every row sees all S_k keys).  The
+ * caller passes the scale; the reference's default is 1/sqrt(D) of the
+ * unpadded head dim.  Runs on the same kernel as mi_stream_fwd.
+ * Replaces dense_attention / prefill_dense / decode_dense
+ * (minference/backend_npu/attention.py:192-211, :243-255, :274-293). */
+int mi_dense_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor4 out, int64_t B, int64_t H,
+                 int64_t S_q, int64_t S_k, int64_t D, int dtype, int causal, float softmax_scale,
+                 void* stream);
 
 /* block_sparse selector: mean-pools q and k over 64-row blocks (block_size
  * must be 64), scores q_pool . k_pool^T * score_scale with future blocks at

@@ -45,3 +45,30 @@ extern "C" int mi_stream_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor
   prm.scale_log2 = softmax_scale * 1.4426950408889634f;
   return launch_attention(q, k, v, out, D, dtype, prm, reinterpret_cast<cudaStream_t>(stream));
 }
+
+extern "C" int mi_dense_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor4 out, int64_t B,
+                            int64_t H, int64_t S_q, int64_t S_k, int64_t D, int dtype, int causal,
+                            float softmax_scale, void* stream) {
+  if (dtype != MI_F16 && dtype != MI_BF16) return MI_ERR_DTYPE;
+  if (D != 64 && D != 96 && D != 128) return MI_ERR_SHAPE;
+  if (B < 0 || H < 0 || S_q < 0 || S_k < 0 || S_k > (1 << 30)) return MI_ERR_SHAPE;
+  if (causal && S_q > S_k) return MI_ERR_SHAPE;  // rows with no visible key
+  if (B > 65535 || H > 65535) return MI_ERR_SHAPE;
+  if (B == 0 || H == 0 || S_q == 0) return MI_OK;
+  if (S_k == 0) return MI_ERR_SHAPE;
+  AttnParams prm{};
+  prm.B = (int)B;
+  prm.H = (int)H;
+  prm.Sq = (int)S_q;
+  prm.Sk = (int)S_k;
+  // Causal: bottom-right aligned, row r sits at absolute position S_k - S_q + r.
+  // Not causal: every row is placed at or past the last key, so the causal
+  // test j <= position passes for every key and only j < S_k bounds the walk.
+  prm.q_off = causal ? (int)(S_k - S_q) : (int)(S_k - 1);
+  prm.T = (int)((S_q + 127) / 128);
+  prm.mode = 0;
+  prm.n_init = 0;
+  prm.n_local = S_k + 1 + (causal ? 0 : S_q);
+  prm.scale_log2 = softmax_scale * 1.4426950408889634f;
+  return launch_attention(q, k, v, out, D, dtype, prm, reinterpret_cast<cudaStream_t>(stream));
+}

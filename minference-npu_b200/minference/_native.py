@@ -73,6 +73,8 @@ def lib() -> ctypes.CDLL:
         L.mi_get_device_error.restype = I
         L.mi_stream_fwd.argtypes = [T4, T4, T4, T4, I64, I64, I64, I64, I64, I, I64, I64, F, P]
         L.mi_stream_fwd.restype = I
+        L.mi_dense_fwd.argtypes = [T4, T4, T4, T4, I64, I64, I64, I64, I64, I, I, F, P]
+        L.mi_dense_fwd.restype = I
         L.mi_block_pool_topk_workspace_size.argtypes = [I64, I64, I64, I64, I64]
         L.mi_block_pool_topk_workspace_size.restype = SZ
         L.mi_block_pool_topk.argtypes = [T4, T4, I64, I64, I64, I64, I64, I, I64, I, F, P, P, SZ, P]

@@ -1,14 +1,14 @@
 """Reference module path kept for drop-in imports (MInference-NPU
-minference/backend_npu/): dense attention and the legacy index converter,
-here running on the sm_100a kernels."""
+minference/backend_npu/): dense / prefill / decode attention and the legacy
+index converter, here running on the sm_100a kernels."""
 
-from ..ops.streaming import dense_attention
+from .attention import decode_dense, dense_attention, is_npu_available, prefill_dense
 from .cuda_shim import convert_vertical_slash_indexes
 
-
-def decode_dense(q, k, v):
-    """q_len == 1 attention over the whole cache (reference attention.py:274)."""
-    return dense_attention(q, k, v, causal=True)
-
-
-__all__ = ["dense_attention", "decode_dense", "convert_vertical_slash_indexes"]
+__all__ = [
+    "dense_attention",
+    "decode_dense",
+    "is_npu_available",
+    "prefill_dense",
+    "convert_vertical_slash_indexes",
+]

@@ -12,7 +12,7 @@ import json
 import os
 import random
 
-from .model2path import MODEL2PATH
+from .model2path import MODEL2PATH, SEEDED_MIXED_MODEL
 
 
 def make(num_layers: int = 32, num_heads: int = 32, seed: int = 0) -> list[dict]:
@@ -33,7 +33,7 @@ def make(num_layers: int = 32, num_heads: int = 32, seed: int = 0) -> list[dict]
 
 
 if __name__ == "__main__":
-    path = MODEL2PATH["microsoft/Phi-3-mini-128k-instruct"]
+    path = MODEL2PATH[SEEDED_MIXED_MODEL]
     with open(path, "w") as f:
         json.dump(make(), f)
     print(path)

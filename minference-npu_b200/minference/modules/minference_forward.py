@@ -34,6 +34,8 @@ from .. import ops as _ops
 
 __all__ = [
     "init_minference_parameters",
+    "sum_all_diagonal_matrix",
+    "_vertical_and_slash_kernel",
     "minference_forward",
     "gather_last_q_sparse_topk",
     "load_pattern_config",
@@ -125,6 +127,35 @@ def group_heads(best_pattern: dict, num_heads: int):
     groups += [(("stream_llm", n, l), hs) for (n, l), hs in stream.items()]
     groups += [(("block_sparse", k), hs) for k, hs in block.items()]
     return groups
+
+
+# ----------------------------------------------------------------------------
+# Reference helpers kept under their names
+# ----------------------------------------------------------------------------
+
+
+def sum_all_diagonal_matrix(mat: torch.Tensor) -> torch.Tensor:
+    """Diagonal sums of ``[B, H, n, m]`` into ``[B, H, n + m - 1]``.
+
+    Output position ``d`` holds the sum of the entries ``mat[..., i, j]`` with
+    ``j - i == d - (n - 1)``: ``d = 0`` is the lone bottom-left entry, the main
+    diagonal lands at ``n - 1`` and the top-right entry at ``n + m - 2``
+    (reference minference/modules/minference_forward.py:124-137).  The VS
+    estimator computes these sums inside ``mi_vs_estimate``; this helper is
+    for callers of the reference's utility."""
+    b, h, n, m = mat.shape
+    rows = torch.arange(n, device=mat.device)
+    cols = torch.arange(m, device=mat.device)
+    slot = (cols[None, :] - rows[:, None] + (n - 1)).expand(b, h, n, m).reshape(b, h, n * m)
+    out = torch.zeros((b, h, n + m - 1), dtype=mat.dtype, device=mat.device)
+    return out.scatter_add_(-1, slot, mat.reshape(b, h, n * m))
+
+
+def _vertical_and_slash_kernel(self, q, k, v, vertical_size, slash_size):
+    """Estimate vertical/slash indices from the last 64 queries, then run the
+    vertical-slash sparse attention (reference minference_forward.py:140-167).
+    ``self`` is unused, as in the reference."""
+    return OPS.vertical_and_slash(q, k, v, vertical_size, slash_size)
 
 
 # ----------------------------------------------------------------------------

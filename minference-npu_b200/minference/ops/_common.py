@@ -29,7 +29,10 @@ def reference_padded_dim(d: int) -> int:
 
 
 def default_softmax_scale(d: int) -> float:
-    """Reference-compatible scale 1/sqrt(padded D); 1/sqrt(D) when MINFERENCE_TRUE_SCALE=1."""
+    """Default scale of the sparse ops: 1/sqrt(padded D), as the reference's
+    sparse ops compute it after zero-padding D; 1/sqrt(D) when
+    MINFERENCE_TRUE_SCALE=1.  Dense attention does not use this: its default
+    is 1/sqrt(D) of the unpadded dim."""
     if os.environ.get(TRUE_SCALE_ENV, "").strip().lower() in {"1", "true", "yes", "on"}:
         return 1.0 / math.sqrt(d)
     return 1.0 / math.sqrt(reference_padded_dim(d))

@@ -7,10 +7,13 @@ minference/ops/streaming_kernel_npu.py:349-397) and ``dense_attention``
 ``j > i - n_local`` (visible set of streaming_kernel_npu.py:131-136).  The
 reference runs a band FA, a sink FA and an eager LSE merge (:233-341); here
 one sm_100a kernel walks the sink blocks and then the band blocks inside a
-single online softmax, so the merge is implicit.
+single online softmax, so the merge is implicit.  Dense attention runs on the
+same kernel with the window covering every key (``mi_dense_fwd``).
 """
 
 from __future__ import annotations
+
+import math
 
 import torch
 
@@ -21,21 +24,21 @@ from ._common import output as _common_out
 __all__ = ["streaming_forward", "dense_attention"]
 
 
-def _launch(q, k, v, n_init: int, n_local: int, softmax_scale: float | None,
+def _launch(q, k, v, n_init: int, n_local: int, scale: float,
             out: torch.Tensor | None = None) -> torch.Tensor:
     check_qkv(q, k, v)
     B, H, S_q, D = q.shape
     S_k = k.shape[2]
     if S_q > S_k:
         raise ValueError(f"S_q={S_q} > S_k={S_k}: rows without any visible key")
-    scale = default_softmax_scale(D) if softmax_scale is None else float(softmax_scale)
     dk = kernel_dim(D)
     qp, kp, vp = prepare(q, dk), prepare(k, dk), prepare(v, dk)
     out = _common_out(out, (B, H, S_q, dk), q)
     with torch.cuda.device(q.device):
         rc = _native.lib().mi_stream_fwd(
             _native.t4(qp), _native.t4(kp), _native.t4(vp), _native.t4(out), B, H, S_q, S_k, dk,
-            _native.dtype_code(q), int(n_init), int(n_local), scale, _native.stream_ptr(q.device),
+            _native.dtype_code(q), int(n_init), int(n_local), float(scale),
+            _native.stream_ptr(q.device),
         )
     _native.check(rc, "mi_stream_fwd")
     return out[..., :D] if dk != D else out
@@ -45,20 +48,42 @@ def streaming_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_init:
                       n_local: int, *, out: torch.Tensor | None = None) -> torch.Tensor:
     """Sink + sliding-window causal attention on BNSD ``[B,H,S,D]`` inputs.
 
-    Same signature and result as the reference; ``k_len <= n_local`` is dense
-    causal attention, which the same kernel computes (window covers all keys).
+    Same signature and result as the reference.  The reference zero-pads D to
+    the next supported head dim before anything else (streaming_kernel_npu.py:
+    377-381), so both the sparse path (:114) and the ``k_len <= n_local``
+    short-circuit to dense causal attention (:386-390) take their default
+    scale from the padded dim: 1/sqrt(128) at D=96.
     """
     n_init = max(0, int(n_init))
     n_local = int(n_local)
+    scale = default_softmax_scale(q.shape[-1])
     if k.shape[2] <= n_local:
-        return dense_attention(q, k, v, causal=True, out=out)
-    return _launch(q, k, v, n_init, n_local, None, out)
+        return dense_attention(q, k, v, scale=scale, causal=True, out=out)
+    return _launch(q, k, v, n_init, n_local, scale, out)
 
 
-def dense_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
-                    softmax_scale: float | None = None, *,
+def dense_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+                    scale: float | None = None, causal: bool = True,
                     out: torch.Tensor | None = None) -> torch.Tensor:
-    """Dense causal attention (the stream kernel with an unbounded window)."""
-    if not causal:
-        raise NotImplementedError("only causal prefill attention is implemented")
-    return _launch(q, k, v, 0, k.shape[2] + 1, softmax_scale, out)
+    """Dense attention on BNSD ``[B,H,S,D]`` inputs (MInference-NPU
+    minference/backend_npu/attention.py:192-211): ``scale`` defaults to
+    ``1/sqrt(D)`` of the unpadded head dim; ``causal`` masks bottom-right
+    aligned (row r sees keys ``j <= S_k - S_q + r``), otherwise every row sees
+    every key.  Output has q's shape, dtype and device; ``out`` (optional) is a
+    caller-owned ``[B,H,S_q,D]`` view written in place."""
+    check_qkv(q, k, v)
+    B, H, S_q, D = q.shape
+    S_k = k.shape[2]
+    if causal and S_q > S_k:
+        raise ValueError(f"S_q={S_q} > S_k={S_k}: causal rows without any visible key")
+    sc = 1.0 / math.sqrt(D) if scale is None else float(scale)
+    dk = kernel_dim(D)
+    qp, kp, vp = prepare(q, dk), prepare(k, dk), prepare(v, dk)
+    out = _common_out(out, (B, H, S_q, dk), q)
+    with torch.cuda.device(q.device):
+        rc = _native.lib().mi_dense_fwd(
+            _native.t4(qp), _native.t4(kp), _native.t4(vp), _native.t4(out), B, H, S_q, S_k, dk,
+            _native.dtype_code(q), 1 if causal else 0, sc, _native.stream_ptr(q.device),
+        )
+    _native.check(rc, "mi_dense_fwd")
+    return out[..., :D] if dk != D else out

@@ -105,6 +105,90 @@ def make_convert_fixture() -> None:
     np.savez_compressed(os.path.join(HERE, "vs_convert.npz"), **out)
 
 
+HF_QK_GAIN = 4.0
+
+
+def tiny_phi3(seed=0, layers=2, heads=4, head_dim=96, qk_gain=HF_QK_GAIN):
+    """Seeded random tiny Phi-3 (same constructor as tests/test_hf_patch.py).
+
+    The q and k rows of every qkv_proj are multiplied by ``qk_gain`` so the
+    attention is peaked enough for the softmax scale and the sparse patterns
+    to change the logits well beyond bf16 rounding."""
+    from transformers import Phi3Config, Phi3ForCausalLM
+
+    torch.manual_seed(seed)
+    cfg = Phi3Config(vocab_size=128, hidden_size=heads * head_dim, intermediate_size=256,
+                     num_hidden_layers=layers, num_attention_heads=heads,
+                     num_key_value_heads=heads, max_position_embeddings=4096,
+                     pad_token_id=0, attn_implementation="eager")
+    model = Phi3ForCausalLM(cfg).eval()
+    with torch.no_grad():
+        for layer in model.model.layers:
+            layer.self_attn.qkv_proj.weight[: 2 * heads * head_dim] *= qk_gain
+    return model
+
+
+HF_MIXED_LAYERS = [
+    {"0": ["stream_llm", 64, 128, 1], "1": ["block_sparse", 4, 0, 1],
+     "2": ["stream_llm", 64, 128, 1], "3": ["dense", 0, 0, 1]},
+    {"0": ["dense", 0, 0, 1], "1": ["vertical_and_slash", 100, 200, 1],
+     "2": ["block_sparse", 4, 0, 1], "3": ["dense", 0, 0, 1]},
+]
+
+
+def make_hf_fixture() -> None:
+    """Logits of a tiny head_dim-96 Phi-3 patched by the reference's own
+    ``MInference`` (models_patch.py) under attn_type "dense" and under a mixed
+    per-head config, computed by its CPU dispatcher in bf16.
+
+    Two shims adapt the reference's forward to the installed transformers
+    (the reference pins 4.57): its ``apply_rotary_pos_emb`` call passes
+    ``position_ids`` in the slot that is now ``unsqueeze_dim``, and it returns
+    a 3-tuple for Phi-3 where the decoder layer now unpacks 2."""
+    import json as _json
+    import tempfile
+
+    _, _, _, fw = _load_ref_package()
+    mp = importlib.import_module("ref_minference.models_patch")
+    out = {}
+    ids = torch.randint(1, 128, (1, 700), generator=torch.Generator().manual_seed(5))
+    out["ids"] = ids.numpy()
+    out["mixed_config"] = np.array(_json.dumps(HF_MIXED_LAYERS))
+    with tempfile.TemporaryDirectory() as td:
+        cfg_path = os.path.join(td, "mixed.json")
+        with open(cfg_path, "w") as f:
+            _json.dump(HF_MIXED_LAYERS, f)
+        for name, kwargs in (("dense", dict(attn_type="dense")),
+                             ("mixed", dict(attn_type="minference", config_path=cfg_path))):
+            model = tiny_phi3().to(torch.bfloat16)
+            out["param_sum"] = np.array(
+                sum(float(p.float().sum()) for p in model.parameters()), dtype=np.float64)
+            with torch.no_grad():
+                out["hf_logits"] = model(ids).logits.float().numpy()
+            mp.MInference(**kwargs)(model)
+            for mod in model.modules():
+                if mod.__class__.__name__ == "Phi3Attention":
+                    fwd = mod.forward
+                    mod.forward = (lambda *a, _f=fwd, **kw: tuple(_f(*a, **kw)[:2]))
+                    mod.init_minference_parameters()
+            # init_minference_parameters has just rebound the module-level
+            # apply_rotary_pos_emb to transformers' own; wrap that one
+            rope = fw.apply_rotary_pos_emb
+            fw.apply_rotary_pos_emb = lambda q, k, c, s, pid=None, _r=rope: _r(q, k, c, s)
+            with torch.no_grad():
+                out[f"{name}_logits"] = model(ids).logits.float().numpy()
+            if name == "dense":
+                # the same run with dense heads at 1/sqrt(padded D): how far a
+                # wrong default scale moves the logits
+                dense = fw.dense_attention
+                fw.dense_attention = lambda q, k, v, causal=True, _d=dense: _d(
+                    q, k, v, causal=causal, scale=1.0 / math.sqrt(128))
+                with torch.no_grad():
+                    out["dense_padded_scale_logits"] = model(ids).logits.float().numpy()
+                fw.dense_attention = dense
+    np.savez_compressed(os.path.join(HERE, "hf_phi3.npz"), **out)
+
+
 def main() -> None:
     bs, st, vs, fw = _load_ref_package()
     torch.set_num_threads(min(8, os.cpu_count() or 1))
@@ -242,11 +326,14 @@ def main() -> None:
     out["n_cases"] = np.array(len(mcases))
     np.savez_compressed(os.path.join(HERE, "vs_mask.npz"), **out)
     make_convert_fixture()
+    make_hf_fixture()
     print("golden fixtures written to", HERE)
 
 
 if __name__ == "__main__":
     if "--only-convert" in sys.argv:
         make_convert_fixture()
+    elif "--only-hf" in sys.argv:
+        make_hf_fixture()
     else:
         main()

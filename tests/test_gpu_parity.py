@@ -98,7 +98,7 @@ def test_stream_golden(cuda):
 def test_dense_causal_matches_sdpa(cuda):
     ops = _ops()
     q, k, v = gen_qkv(1, 4, 2048, 96, torch.bfloat16, 5, device=cuda)
-    out = ops.dense_attention(q, k, v, causal=True, softmax_scale=96 ** -0.5)
+    out = ops.dense_attention(q, k, v, causal=True)  # default scale 1/sqrt(D)
     ref = torch.nn.functional.scaled_dot_product_attention(
         q.float(), k.float(), v.float(), is_causal=True, scale=96 ** -0.5
     )
@@ -205,7 +205,7 @@ def test_block_sparse_full_topk_is_dense(cuda):
     ops = _ops()
     q, k, v = gen_qkv(1, 2, 1536, 96, torch.bfloat16, 9, device=cuda)
     a = ops.block_sparse_attention(q, k, v, 10_000)
-    b = ops.dense_attention(q, k, v)
+    b = ops.dense_attention(q, k, v, scale=128 ** -0.5)  # block_sparse: padded-D scale
     assert (a.float() - b.float()).abs().max().item() < 1e-6
 
 
