@@ -92,6 +92,7 @@ int mi_dense_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor4 out, int64
  * index) and writes them in ascending order to out_idx, int64
  * [B, H, ceil(S_q/64), min(topk, ceil(S_k/64))], contiguous.
  * force_sink_diag != 0 additionally forces block 0 and the diagonal block in.
+ * The workspace size is SIZE_MAX for negative or overflowing sizes.
  * Replaces _select_block_sparse_topk_indices (block_sparse_kernel_npu.py:230). */
 size_t mi_block_pool_topk_workspace_size(int64_t B, int64_t H, int64_t S_q, int64_t S_k,
                                          int64_t D);

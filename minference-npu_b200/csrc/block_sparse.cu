@@ -298,10 +298,25 @@ int launch_attention(const mi_tensor4& q, const mi_tensor4& k, const mi_tensor4&
 
 using namespace mib200;
 
+// Bytes of one pooled tensor (4-byte floats, B*H*nb*D of them), or SIZE_MAX
+// when an argument is negative or the product does not fit in size_t.
+static size_t pooled_bytes(int64_t B, int64_t H, int64_t nb, int64_t D) {
+  if (B < 0 || H < 0 || nb < 0 || D < 0) return SIZE_MAX;
+  unsigned __int128 n = (unsigned __int128)B * (uint64_t)H;
+  n *= (uint64_t)nb;
+  n *= (uint64_t)D;
+  n *= sizeof(float);
+  if (n > (unsigned __int128)(SIZE_MAX / 2)) return SIZE_MAX;
+  return align_up((size_t)n);
+}
+
 extern "C" size_t mi_block_pool_topk_workspace_size(int64_t B, int64_t H, int64_t S_q,
                                                     int64_t S_k, int64_t D) {
+  if (S_q < 0 || S_k < 0 || S_q > ((int64_t)1 << 40) || S_k > ((int64_t)1 << 40)) return SIZE_MAX;
   const int64_t nbq = (S_q + 63) / 64, nbk = (S_k + 63) / 64;
-  return align_up(sizeof(float) * B * H * nbq * D) + align_up(sizeof(float) * B * H * nbk * D);
+  const size_t a = pooled_bytes(B, H, nbq, D), b = pooled_bytes(B, H, nbk, D);
+  if (a == SIZE_MAX || b == SIZE_MAX) return SIZE_MAX;
+  return a + b;
 }
 
 extern "C" int mi_block_pool_topk(mi_tensor4 q, mi_tensor4 k, int64_t B, int64_t H, int64_t S_q,

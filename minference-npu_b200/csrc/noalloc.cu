@@ -50,7 +50,12 @@ extern "C" int mi_block_pool_topk_noalloc(mi_tensor4 q, mi_tensor4 k, int64_t B,
                                           int64_t S_q, int64_t S_k, int64_t D, int dtype,
                                           int64_t topk, int force_sink_diag, float score_scale,
                                           int64_t* out_idx, void* stream) {
+  // Argument checks first, so a bad shape reports MI_ERR_SHAPE / MI_ERR_DTYPE
+  // rather than looking like a size beyond the scratch.
+  if (dtype != MI_F16 && dtype != MI_BF16) return MI_ERR_DTYPE;
+  if (B < 0 || H < 0 || S_q < 0 || S_k < 0 || D <= 0 || D > 128 || topk < 1) return MI_ERR_SHAPE;
   const size_t need = mi_block_pool_topk_workspace_size(B, H, S_q, S_k, D);
+  if (need == SIZE_MAX) return MI_ERR_SHAPE;
   if (need > mib200::kNoAllocScratchBytes) return MI_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;
   const int rc = mib200::noalloc_scratch_ptr(&scratch);

@@ -207,6 +207,47 @@ def vs_mask(v_idx: np.ndarray, s_idx: np.ndarray, S: int) -> np.ndarray:
     return tok & causal_mask(S, S)
 
 
+# ---------------------------------------------------------------------------
+# The same visible sets for selected query rows only: [len(rows), S_k].  For
+# parity checks at sizes where an [S, S] mask does not fit (64K-128K).
+# ---------------------------------------------------------------------------
+
+
+def stream_rows_mask(rows, S_q: int, S_k: int, n_init: int, n_local: int) -> np.ndarray:
+    abs_i = (np.asarray(rows, dtype=np.int64) + (S_k - S_q))[:, None]
+    j = np.arange(S_k)[None, :]
+    return ((j < n_init) | (j > abs_i - n_local)) & (j <= abs_i)
+
+
+def block_sparse_rows_mask(block_idx: np.ndarray, S: int, rows) -> np.ndarray:
+    """block_idx: [nb, topk] (one head); rows sees the blocks of its query block."""
+    rows = np.asarray(rows, dtype=np.int64)
+    nb = -(-S // 64)
+    out = np.zeros((len(rows), S), dtype=bool)
+    for n, r in enumerate(rows):
+        for kb in block_idx[r // 64]:
+            if 0 <= kb < nb:
+                out[n, kb * 64:min(S, kb * 64 + 64)] = True
+    return out & (np.arange(S)[None, :] <= rows[:, None])
+
+
+def vs_rows_mask(v_idx: np.ndarray, s_idx: np.ndarray, S: int, rows) -> np.ndarray:
+    """v_idx [nv], s_idx [ns] (one head); the direct-mask row of each row's query block."""
+    v = np.ascontiguousarray(v_idx, dtype=np.int32)
+    s = np.ascontiguousarray(s_idx, dtype=np.int32)
+    rows = np.asarray(rows, dtype=np.int64)
+    cache = {}
+    out = np.zeros((len(rows), S), dtype=bool)
+    for n, r in enumerate(rows):
+        bq = int(r // 64)
+        if bq not in cache:
+            b = np.zeros(S, dtype=np.uint8)
+            lib().oracle_vs_block_row(_ptr(v), len(v), _ptr(s), len(s), S, bq, _ptr(b))
+            cache[bq] = b.astype(bool)
+        out[n] = cache[bq]
+    return out & (np.arange(S)[None, :] <= rows[:, None])
+
+
 def masked_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, mask: np.ndarray,
                      scale: float) -> np.ndarray:
     """fp32 softmax(q k^T * scale, masked) v for one head; fully masked rows -> 0."""

@@ -220,7 +220,7 @@ def _golden_hf():
 
 def _phi3_for_golden(g):
     model = tiny_phi3(qk_gain=4.0).to(torch.bfloat16)
-    psum = sum(float(p.float().sum()) for p in model.parameters())
+    psum = sum(float(p.detach().float().sum()) for p in model.parameters())
     assert abs(psum - float(g["param_sum"])) < 1e-3 * max(1.0, abs(psum)), \
         "seeded tiny Phi-3 weights differ from the ones the fixture was made with"
     return model

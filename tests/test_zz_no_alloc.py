@@ -83,8 +83,19 @@ def test_noalloc_rejects_sizes_beyond_scratch(capi, cuda):
     _native, lib, noalloc = capi
     limit = lib.mi_block_pool_topk_noalloc_limit()
     B, H, D = 1, 64, 128
-    S = 65536  # pooled q + k: 64 heads * 2048 blocks * 128 * 4 B = 64 MiB > 32 MiB
+    S = 65536  # pooled q (32 MiB) + pooled k^T (32 MiB) = 64 MiB > 32 MiB
     assert lib.mi_block_pool_topk_workspace_size(B, H, S, S, D) > limit
     t = _native.mi_tensor4(0, 0, 0, 0, 1)
     rc = noalloc(t, t, B, H, S, S, D, 1, 10, 0, 0.1, None, None)
     assert rc == 7  # MI_ERR_SCRATCH_LIMIT, before any device work
+
+
+def test_noalloc_reports_bad_shapes_as_shape_errors(capi, cuda):
+    """Negative or overflowing sizes are argument errors (MI_ERR_SHAPE), not
+    scratch-limit refusals."""
+    _native, lib, noalloc = capi
+    t = _native.mi_tensor4(0, 0, 0, 0, 1)
+    assert noalloc(t, t, 1, -4, 1024, 1024, 96, 1, 10, 0, 0.1, None, None) == 1
+    assert noalloc(t, t, -1, 4, 1024, 1024, 96, 1, 10, 0, 0.1, None, None) == 1
+    assert noalloc(t, t, 1 << 40, 1 << 20, 1 << 30, 1 << 30, 96, 1, 10, 0, 0.1, None, None) == 1
+    assert lib.mi_block_pool_topk_workspace_size(1, -4, 1024, 1024, 96) == 2 ** 64 - 1
