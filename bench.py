@@ -364,84 +364,255 @@ def _peaks(sustained: bool = False):
         return (1400.0 if sustained else 1590.0), 6650.0, "fallback"
 
 
-def cpu_reference_sample(S: int, budget_s: float = 12.0) -> dict:
-    """The reference's CPU algorithm (oracle port: fp32 masked attention over
-    the full key range per query row, as the reference's PyTorch paths do),
-    timed on a bounded sample of query rows and extrapolated to the layer."""
-    from oracle import oracle as O
+# ---------------------------------------------------------------------------
+# the reference's CPU path (reference arm and cpu_baseline)
+# ---------------------------------------------------------------------------
+REF_INSTALL = os.path.join(ROOT, "baseline", "_ref")
 
-    # All the host cores this process may use, for numpy's BLAS (the masked
-    # attention's matmuls) and torch: launchers such as torchrun set
-    # OMP_NUM_THREADS=1, which would time a single-threaded CPU.
-    ncores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
-    torch.set_num_threads(ncores)
-    try:
-        from threadpoolctl import threadpool_info, threadpool_limits
 
-        limiter = threadpool_limits(limits=ncores)
-        blas = [d.get("num_threads", 1) for d in threadpool_info()
-                if d.get("user_api") == "blas"]
-        threads = max(blas) if blas else torch.get_num_threads()
-    except Exception:  # noqa: BLE001
-        limiter = None
-        threads = torch.get_num_threads()
-    rng = np.random.default_rng(0)
-    pats = head_patterns()
-    rows_total = 0
-    t_total = 0.0
-    # one head of each pattern, a 64-row query block at a few positions
-    for p in ("vertical_and_slash", "block_sparse", "stream_llm"):
-        q, k, v = make_inputs([pats.index(p)], S, "cpu")
-        qf, kf, vf = q[0, 0].float().numpy(), k[0, 0].float().numpy(), v[0, 0].float().numpy()
-        qb, kb = q[0, 0:1][None], k[0, 0:1][None]
-        for bq in (S // 64 - 1, S // 128, S // 256):
-            r0 = bq * 64
-            rows = slice(r0, r0 + 64)
+def _load_reference_package():
+    """The reference package installed (unmodified, by pip) under
+    baseline/_ref, imported as ``ref_minference`` so it cannot shadow this
+    build's own ``minference``.  None when it is not installed."""
+    import importlib
+    import importlib.util
+
+    pkg = os.path.join(REF_INSTALL, "minference")
+    if not os.path.isfile(os.path.join(pkg, "__init__.py")):
+        return None
+    if "ref_minference" not in sys.modules:
+        spec = importlib.util.spec_from_file_location(
+            "ref_minference", os.path.join(pkg, "__init__.py"), submodule_search_locations=[pkg])
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules["ref_minference"] = mod
+        spec.loader.exec_module(mod)
+    return tuple(importlib.import_module(f"ref_minference.{m}") for m in (
+        "ops.block_sparse_kernel_npu", "ops.streaming_kernel_npu",
+        "ops.vertical_slash_kernel_npu", "modules.minference_forward"))
+
+
+def _host_threads() -> int:
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    # launchers such as torchrun set OMP_NUM_THREADS=1; the CPU path gets every core
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
+
+
+class RefCpuLayer:
+    """The bench layer (same 32-head pattern mix, S, input distribution) on
+    the host cores, computed the way the reference's CPU path computes it.
+
+    Index estimation runs once per head before any timing, through the
+    reference's own functions: ``_vertical_and_slash_kernel``
+    (modules/minference_forward.py:140-167; its attention call is captured,
+    not run) and ``_select_block_sparse_topk_indices``
+    (ops/block_sparse_kernel_npu.py:230-263) on D zero-padded to 128, as
+    ``block_sparse_attention`` pads first.  Its time is reported, not timed
+    into the steps.
+
+    A step takes one 64-row query block of each of the 32 heads (positions
+    cycle through the sequence from step to step):
+    * stream_llm heads call the reference's ``_streaming_pytorch_ref``
+      (ops/streaming_kernel_npu.py:94-146) on that block with the keys up to
+      its last row (the rows' absolute positions are then exact);
+    * block_sparse and vertical_and_slash heads evaluate the reference's
+      masked attention (``_block_sparse_pytorch_ref`` :325-348,
+      ``_vertical_slash_pytorch_ref`` vertical_slash_kernel_npu.py:377-415:
+      fp32 logits over all keys, masked softmax, nan_to_num, PV) for the
+      block's rows only, with the block's rows of the token mask built by the
+      reference's rules (:266-317, direct mask :255-369).  The reference
+      materialises [S, S] fp32 logits per head (17 GB at 64K); this chunks
+      them by query rows.
+    Everything runs at D padded to 128, as the reference pads before these
+    calls; k and v are converted to fp32 once, outside the timing.
+
+    kind "reference" uses the package installed under baseline/_ref; kind
+    "port" (when it is absent) uses the C oracle's estimators and the same
+    chunked math."""
+
+    def __init__(self, S: int, n_heads: int = H_TOTAL):
+        import torch.nn.functional as F
+
+        self.S, self.nb = S, S // 64
+        self.threads = _host_threads()
+        ref = _load_reference_package()
+        self.kind = "reference" if ref is not None else "port"
+        self.pats = head_patterns(n_heads)
+        self.heads = []
+        est_s = {"vertical_and_slash": [], "block_sparse": []}
+        for h in range(n_heads):
+            q, k, v = make_inputs([h], S, "cpu")
+            p = self.pats[h]
+            qp, kp, vp = (F.pad(t, (0, 128 - D)) for t in (q, k, v))
+            ent = {"p": p, "q": qp, "k": kp, "kf": kp[0, 0].float(), "vf": vp[0, 0].float(),
+                   "v": vp}
             t0 = time.perf_counter()
-            if p == "stream_llm":
-                mask = O.stream_mask(S, S, ST_INIT, ST_LOCAL)[rows] if S <= 16384 else None
-                abs_i = np.arange(r0, r0 + 64)[:, None]
-                j = np.arange(S)[None, :]
-                mask = ((j < ST_INIT) | ((j <= abs_i) & (j > abs_i - ST_LOCAL))) & (j <= abs_i)
+            if p == "vertical_and_slash":
+                ent["vis_cols"], ent["s_idx"] = self._vs_indices(ref, q, k, v)
+            elif p == "block_sparse":
+                ent["blk"] = self._bs_indices(ref, qp, kp)
+            if p in est_s:
+                est_s[p].append(time.perf_counter() - t0)
+            self.heads.append(ent)
+        self.ref = ref
+        self.est_s_per_head = {p: statistics.mean(t) for p, t in est_s.items() if t}
+        self.step_no = 0
+
+    @staticmethod
+    def _vs_indices(ref, q, k, v):
+        if ref is None:
+            from oracle import oracle as O
+
+            vi, si = O.vs_estimate(q, k, VS_V, VS_S)
+            vi, si = torch.from_numpy(vi)[0, 0], torch.from_numpy(si)[0, 0]
+        else:
+            fw = ref[3]
+            cap = {}
+
+            def capture(q_, k_, v_, v_idx, s_idx):
+                cap["v"], cap["s"] = v_idx, s_idx
+                return q_
+
+            saved = fw._vs_sparse_attention
+            fw._vs_sparse_attention = capture
+            try:
+                fw._vertical_and_slash_kernel(None, q, k, v, VS_V, VS_S)
+            finally:
+                fw._vs_sparse_attention = saved
+            vi, si = cap["v"][0, 0], cap["s"][0, 0]
+        S = q.shape[2]
+        vert = torch.zeros(S, dtype=torch.bool)
+        vert[vi.long().clamp(0, S - 1)] = True
+        return vert, si.long()
+
+    @staticmethod
+    def _bs_indices(ref, qp, kp):
+        if ref is None:
+            from oracle import oracle as O
+
+            idx = torch.from_numpy(O.block_pool_topk(qp, kp, BS_TOPK, 128 ** -0.5))
+        else:
+            idx = ref[0]._select_block_sparse_topk_indices(qp, kp, BS_TOPK, 64)
+        nb = idx.shape[2]
+        blk = torch.zeros(nb, nb, dtype=torch.bool)
+        blk.scatter_(1, idx[0, 0].clamp(0, nb - 1), True)
+        return blk
+
+    def _rows_visible(self, ent, r0: int) -> torch.Tensor:
+        S = self.S
+        j = torch.arange(S)
+        i = torch.arange(r0, r0 + 64)
+        if ent["p"] == "block_sparse":
+            tok = ent["blk"][r0 // 64].repeat_interleave(64)[:S]
+        else:  # direct VS mask: slash ranges [re-64, re) of this query block, OR verticals
+            end_m = r0 + 64
+            s = ent["s_idx"]
+            s = s[s < end_m]
+            re = (end_m - s).clamp(min=64).clamp(max=S)
+            delta = torch.zeros(S + 1, dtype=torch.int32)
+            delta.scatter_add_(0, (re - 64).clamp(min=0), torch.ones_like(re, dtype=torch.int32))
+            delta.scatter_add_(0, re, -torch.ones_like(re, dtype=torch.int32))
+            tok = (delta.cumsum(0)[:S] > 0) | ent["vis_cols"]
+        return tok[None, :] & (j[None, :] <= i[:, None])
+
+    def step(self) -> float:
+        """One step; returns its dense-causal-equivalent FLOPs (D = 96)."""
+        scale = 128 ** -0.5
+        flops = 0.0
+        for h, ent in enumerate(self.heads):
+            bq = (h * self.nb // len(self.heads) + self.step_no * 17) % self.nb
+            r0 = bq * 64
+            if ent["p"] == "stream_llm":
+                st = self.ref[1] if self.ref is not None else None
+                q, k, v = (ent["q"][:, :, r0:r0 + 64], ent["k"][:, :, :r0 + 64],
+                           ent["v"][:, :, :r0 + 64])
+                if st is not None:
+                    st._streaming_pytorch_ref(q, k, v, ST_INIT, ST_LOCAL)
+                else:
+                    from oracle import oracle as O
+
+                    mask = O.stream_rows_mask(np.arange(r0, r0 + 64), 64, r0 + 64, ST_INIT,
+                                              ST_LOCAL)
+                    O.masked_attention(q[0, 0].float().numpy(), k[0, 0].float().numpy(),
+                                       v[0, 0].float().numpy(), mask, scale)
             else:
-                j = np.arange(S)[None, :]
-                abs_i = np.arange(r0, r0 + 64)[:, None]
-                mask = j <= abs_i  # visible-set construction cost is excluded (favours the CPU)
-            O.masked_attention(qf[rows], kf, vf, mask, 128 ** -0.5)
-            t_total += time.perf_counter() - t0
-            rows_total += 64
-            if t_total > budget_s:
-                break
-    per_row = t_total / max(rows_total, 1)
-    layer_s = per_row * S * H_TOTAL
-    if limiter is not None:
-        limiter.restore_original_limits()
-    return {"layer_s": layer_s, "cores": threads, "rows": rows_total, "seconds": t_total}
+                vis = self._rows_visible(ent, r0)
+                logits = (ent["q"][0, 0, r0:r0 + 64].float() @ ent["kf"].T) * scale
+                logits.masked_fill_(~vis, float("-inf"))
+                probs = torch.nan_to_num(torch.softmax(logits, dim=-1), nan=0.0)
+                (probs @ ent["vf"]).to(torch.bfloat16)
+            flops += 4.0 * D * sum(range(r0 + 1, r0 + 65))
+        self.step_no += 1
+        return flops
+
+    def describe(self) -> str:
+        fn = ("reference functions (baseline/_ref): _vertical_and_slash_kernel, "
+              "_select_block_sparse_topk_indices, _streaming_pytorch_ref; masked attention of "
+              "_block_sparse_pytorch_ref / _vertical_slash_pytorch_ref chunked by 64 query rows"
+              if self.kind == "reference" else
+              "oracle port: C-oracle estimators, fp32 masked attention chunked by 64 query rows")
+        est = ", ".join(f"{p} {t:.2f} s/head" for p, t in self.est_s_per_head.items())
+        return (f"per step one 64-row query block of each of the {len(self.heads)} heads at "
+                f"S={self.S} (positions cycle over the sequence), fp32, D padded to 128; "
+                f"{fn}; index estimation once per head before timing ({est})")
+
+    def layer_estimate_s(self, step_s: float) -> float:
+        """Extrapolation (labelled, not a measurement): a whole layer is nb
+        steps' worth of query blocks plus index estimation for every head."""
+        est = sum(self.est_s_per_head.get(e["p"], 0.0) for e in self.heads)
+        return step_s * self.nb + est
+
+
+def time_reference_cpu(S: int, steps: int, warmup: int, layer=None):
+    """(seconds per step, dense-causal FLOPs per step, layer) for the
+    reference's CPU path; FLOPs are averaged over the timed steps."""
+    layer = layer or RefCpuLayer(S)
+    for _ in range(warmup):
+        layer.step()
+    t0 = time.perf_counter()
+    fl = 0.0
+    for _ in range(steps):
+        fl += layer.step()
+    dt = time.perf_counter() - t0
+    return dt / steps, fl / steps, layer
+
+
+def bench_config(args, S: int, world: int, split_gather: bool = False) -> dict:
+    return {"workload": "phi3-mini layer attention, mixed patterns (40% VS v=1000 s=6096, "
+                        "40% block_sparse top-100, 20% stream 128+1024)",
+            "model": "Phi-3-mini-128k attention shape", "global_batch": 1, "seq_len": S,
+            "heads": args.heads, "head_dim": D, "pattern": args.pattern,
+            "parallelism": f"head-shard{world}" if world > 1 else "single",
+            "gather": ("all-gather in two halves by local head, the first overlapped "
+                       "with the remaining attention" if split_gather else
+                       ("one all-gather" if world > 1 else "none")),
+            "head_map": args.head_map if world > 1 else "single",
+            "o_proj": args.o_proj if world > 1 else "none",
+            "l2": "inputs 1.2 GB > L2 (no flush needed)"}
 
 
 def run_reference_arm(args, rank, world) -> None:
+    """The reference's CPU path on this host's cores, rank 0 only (other ranks
+    exit without work).  Each step is a bounded sample of the bench layer
+    (RefCpuLayer); ms_per_step is the measured time of that sample."""
     if rank != 0:
         return
     S = args.seq
-    times = []
-    info = None
-    for i in range(args.warmup + args.steps):
-        info = cpu_reference_sample(S, budget_s=max(2.0, 20.0 / (args.steps + args.warmup)))
-        if i >= args.warmup:
-            times.append(info["layer_s"])
-    layer_s = statistics.mean(times)
-    val = dense_causal_flops(S, H_TOTAL) / layer_s / 1e12
-    sample = (f"{info['rows']} query rows per step (64-row blocks of one head of each pattern), "
-              f"fp32 masked attention over all keys, extrapolated to S={S} x {H_TOTAL} heads")
+    step_s, flops, layer = time_reference_cpu(S, args.steps, args.warmup)
+    val = flops / step_s / 1e12
+    sample = layer.describe()
     line = {
         "metric": METRIC, "value": val, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": layer_s * 1e3,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": "phi3-mini layer attention, mixed patterns",
-                                        "seq_len": S, "heads": H_TOTAL, "head_dim": D},
-        "cpu_baseline": {"value": val, "unit": UNIT, "cores": info["cores"], "kind": "port",
+        "data": "synthetic (seeded N(0,1)/sqrt(96), rank-4 K bias, x4 sink keys; CPU generator)",
+        "config": bench_config(args, S, world),
+        "cpu_baseline": {"value": val, "unit": UNIT, "cores": layer.threads, "kind": layer.kind,
                          "sample": sample},
         "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "extrapolated_layer_ms": {"value": layer.layer_estimate_s(step_s) * 1e3,
+                                  "note": "not measured: step time x 1024 blocks + index "
+                                          "estimation of every head"},
     }
     print(json.dumps(line), flush=True)
 
@@ -856,22 +1027,47 @@ def main():
     d1.record()
     barrier()
     dense_ms = max_over_ranks(d0.elapsed_time(d1) / d_steps)
+    # comparator only: torch SDPA (cuDNN's sm100 flash kernel where available)
+    # on the same heads; never on this build's path
+    sdpa_ms, sdpa_backend = None, None
+    try:
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+
+        for backend in (SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION,
+                        SDPBackend.EFFICIENT_ATTENTION):
+            try:
+                with sdpa_kernel([backend]):
+                    torch.nn.functional.scaled_dot_product_attention(
+                        layer.q, layer.k, layer.v, is_causal=True, scale=D ** -0.5)
+                    barrier()
+                    d0.record()
+                    for _ in range(d_steps):
+                        torch.nn.functional.scaled_dot_product_attention(
+                            layer.q, layer.k, layer.v, is_causal=True, scale=D ** -0.5)
+                    d1.record()
+                    barrier()
+                sdpa_ms, sdpa_backend = max_over_ranks(d0.elapsed_time(d1) / d_steps), backend.name
+                break
+            except RuntimeError:
+                continue
+    except Exception:  # noqa: BLE001
+        pass
+    best_dense_ms = min(dense_ms, sdpa_ms) if sdpa_ms else dense_ms
 
     err = _native.device_error()
-    # The attention launches are timed inside a run of args.steps back-to-back
-    # layer steps, where the GPU settles under its power cap: the sustained peak.
-    tf_peak, _, peak_kind = _peaks(sustained=True)
+    # The timed region is well under a second (args.steps layers of ~16 ms), too
+    # short for the GPU to settle under its power cap: the burst peak applies.
+    tf_peak, _, peak_kind = _peaks(sustained=False)
     # achieved over the attention phase of each group (plan kernels included)
     achieved = alg_flops_rank / (attn_ms * 1e-3) / 1e12
 
     cpu_base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.pattern == "mixed":
-        info = cpu_reference_sample(S)
-        cpu_val = dense_flops / info["layer_s"] / 1e12
-        cpu_base = {"value": cpu_val, "unit": UNIT, "cores": info["cores"], "kind": "port",
-                    "sample": (f"{info['rows']} query rows (64-row blocks of one head per pattern), "
-                               f"fp32 masked attention over all keys, {info['seconds']:.1f} s, "
-                               f"extrapolated to S={S} x {H_TOTAL} heads")}
+        step_s, flops, ref_layer = time_reference_cpu(S, steps=3, warmup=1)
+        cpu_val = flops / step_s / 1e12
+        cpu_base = {"value": cpu_val, "unit": UNIT, "cores": ref_layer.threads,
+                    "kind": ref_layer.kind, "sample": ref_layer.describe() + "; 3 timed steps",
+                    "ms_per_step": step_s * 1e3}
 
     if rank == 0:
         line = {
@@ -879,20 +1075,14 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1)/sqrt(96), rank-4 K bias, x4 sink keys)",
-            "config": {"workload": "phi3-mini layer attention, mixed patterns (40% VS v=1000 s=6096, "
-                                   "40% block_sparse top-100, 20% stream 128+1024)",
-                       "model": "Phi-3-mini-128k attention shape", "global_batch": 1, "seq_len": S,
-                       "heads": n_heads, "head_dim": D, "pattern": args.pattern,
-                       "parallelism": f"head-shard{world}" if world > 1 else "single",
-                       "gather": ("all-gather in two halves by local head, the first overlapped "
-                                  "with the remaining attention" if split_gather else
-                                  ("one all-gather" if world > 1 else "none")),
-                       "head_map": args.head_map if world > 1 else "single",
-                       "o_proj": args.o_proj if world > 1 else "none",
-                       "l2": "inputs 1.2 GB > L2 (no flush needed)"},
+            "config": bench_config(args, S, world, split_gather),
             "ms_per_layer": ms,
             "dense_ms_per_layer": dense_ms,
-            "speedup_vs_dense": dense_ms / ms,
+            "sdpa_dense_ms_per_layer": sdpa_ms,
+            "sdpa_backend": sdpa_backend,
+            "speedup_vs_dense": best_dense_ms / ms,
+            "speedup_vs_dense_note": "against the faster of this build's dense kernel and torch "
+                                     "SDPA on the same heads",
             "attn_phase_ms": attn_ms,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf_peak,
                          "unit": "TFLOP/s", "frac": achieved / tf_peak,
