@@ -109,36 +109,42 @@ def make_inputs(heads: list[int], S: int, device, dtype=torch.bfloat16):
 # ---------------------------------------------------------------------------
 # visible-pair counts (algorithmic work) from the selected indices
 # ---------------------------------------------------------------------------
-def stream_visible_pairs(S: int, n_init: int, n_local: int) -> int:
-    i = np.arange(S, dtype=np.int64)
+def stream_visible_pairs(S: int, n_init: int, n_local: int, rows=None) -> int:
+    r0, r1 = rows if rows is not None else (0, S)
+    i = np.arange(r0, r1, dtype=np.int64)
     sink = np.minimum(i + 1, n_init)
     band = np.maximum(0, (i + 1) - np.maximum(n_init, i - n_local + 1))
     return int((sink + band).sum())
 
 
-def bs_visible_pairs(idx: torch.Tensor, S: int) -> int:
-    """idx [nb, topk] one head, S multiple of 64."""
+def bs_visible_pairs(idx: torch.Tensor, S: int, rows=None) -> int:
+    """idx [nb, topk] one head, S multiple of 64; query rows [r0, r1) (64-aligned)."""
+    r0, r1 = rows if rows is not None else (0, S)
     nb = idx.shape[0]
     bq = torch.arange(nb, device=idx.device)[:, None]
     sel = torch.zeros(nb, nb, dtype=torch.bool, device=idx.device)
     sel.scatter_(1, idx.clamp(0, nb - 1), True)
     kb = torch.arange(nb, device=idx.device)[None, :]
     sel &= kb <= bq
-    off = (sel & (kb < bq)).sum().item() * 64 * 64
-    diag = sel.diagonal().sum().item() * (64 * 65 // 2)
+    sel = sel[r0 // 64:r1 // 64]
+    kb = kb[:, :]
+    bqr = bq[r0 // 64:r1 // 64]
+    off = (sel & (kb < bqr)).sum().item() * 64 * 64
+    diag = (sel & (kb == bqr)).sum().item() * (64 * 65 // 2)
     return int(off + diag)
 
 
-def vs_visible_pairs(v_idx: torch.Tensor, s_idx: torch.Tensor, S: int) -> int:
-    """Direct-mask semantics (slash ranges OR vertical columns) AND causal; S % 64 == 0."""
+def vs_visible_pairs(v_idx: torch.Tensor, s_idx: torch.Tensor, S: int, rows=None) -> int:
+    """Direct-mask semantics (slash ranges OR vertical columns) AND causal; S % 64 == 0;
+    query rows [r0, r1) (64-aligned)."""
     dev = v_idx.device
-    nb = S // 64
+    r0, r1 = rows if rows is not None else (0, S)
     s = s_idx.long()
     total = 0
     vert = torch.zeros(S, dtype=torch.bool, device=dev)
     vert[v_idx.long().clamp(0, S - 1)] = True
-    for c0 in range(0, nb, 128):
-        bq = torch.arange(c0, min(nb, c0 + 128), device=dev)
+    for c0 in range(r0 // 64, r1 // 64, 128):
+        bq = torch.arange(c0, min(r1 // 64, c0 + 128), device=dev)
         end_m = (bq + 1) * 64
         valid = s[None, :] < end_m[:, None]
         re = (end_m[:, None] - s[None, :]).clamp(min=64).clamp(max=S)
@@ -329,6 +335,129 @@ class Layer:
                 tot += stream_visible_pairs(self.S, ST_INIT, ST_LOCAL) * (sl.stop - sl.start)
             else:
                 tot += self.S * (self.S + 1) // 2 * (sl.stop - sl.start)
+        return tot
+
+
+class TileLayer:
+    """One rank's share of the layer under the (head, query-tile) partition
+    (minference.sharding.tile_partition): a contiguous range of the layer's
+    (head, 128-row tile) units of equal modelled cost.  Heads are laid out
+    grouped by pattern (cheapest first), the order a one-time permutation of
+    the QKV / o_proj weights gives.  The rank holds q/k/v of the heads its
+    range touches and a full [1, H, S, D] output; its range is a contiguous
+    block of that output.  A step runs the first half (by cost) of the range,
+    starts exchanging it with every peer on a side stream, runs the second
+    half, then exchanges that."""
+
+    def __init__(self, rank, world, S, device, pattern="mixed", n_heads=H_TOTAL):
+        from minference import ops
+        from minference.sharding import tile_partition, unit_range_split
+
+        self.ops, self.S, self.device, self.rank, self.world = ops, S, device, rank, world
+        pats = head_patterns(n_heads) if pattern == "mixed" else [pattern] * n_heads
+        order = ("stream_llm", "block_sparse", "vertical_and_slash", "dense")
+        self.layout = sorted(range(n_heads), key=lambda h: (order.index(pats[h]), h))
+        self.slot_pat = [pats[h] for h in self.layout]
+        keys = [PATTERN_KEYS[p] for p in self.slot_pat]
+        self.parts = tile_partition(keys, S, world)
+        self.halves = [unit_range_split(pr, keys, S) for pr in self.parts]
+        mine = self.parts[rank]
+        self.slots = sorted({pc.slot for pc in mine})
+        self.local = {sl: i for i, sl in enumerate(self.slots)}
+        self.heads = [self.layout[sl] for sl in self.slots]
+        self.q, self.k, self.v = make_inputs(self.heads, S, device)
+        self.out = torch.zeros(1, n_heads, S, D, dtype=torch.bfloat16, device=device)
+        self.comm = torch.cuda.Stream(device=device)
+
+    def _batches(self, pieces):
+        """Consecutive whole-head pieces of one pattern run as one launch
+        over a head range; partial heads run as row windows."""
+        S = self.S
+        batches = []
+        for pc in pieces:
+            full = pc.rows(S) == (0, S)
+            p = self.slot_pat[pc.slot]
+            if (batches and full and batches[-1][2] and batches[-1][0] == p
+                    and batches[-1][1][-1] + 1 == pc.slot):
+                batches[-1][1].append(pc.slot)
+            else:
+                batches.append([p, [pc.slot], full, pc.rows(S)])
+        return batches
+
+    def _run_pieces(self, pieces, est, q, k, v, ev):
+        ops = self.ops
+        for p, slots, _full, rows in self._batches(pieces):
+            a, b = self.local[slots[0]], self.local[slots[-1]] + 1
+            qs, ks, vs = q[:, a:b], k[:, a:b], v[:, a:b]
+            os_ = self.out[:, slots[0]:slots[-1] + 1]
+            rw = None if rows == (0, self.S) else rows
+            key = (slots[0], len(slots))
+            if p == "vertical_and_slash":
+                if key not in est:
+                    est[key] = ops.vertical_and_slash_estimate(qs, ks, VS_V, VS_S)
+                vi, si = est[key]
+                e0 = Layer._ev(ev)
+                ops.vertical_slash_sparse_attention(qs, ks, vs, vi, si, out=os_, rows=rw)
+            elif p == "block_sparse":
+                if key not in est:
+                    est[key] = ops.select_block_sparse_topk_indices(qs, ks, BS_TOPK)
+                e0 = Layer._ev(ev)
+                ops.block_sparse_attention_from_indices(qs, ks, vs, est[key], out=os_, rows=rw)
+            elif p == "stream_llm":
+                e0 = Layer._ev(ev)
+                ops.streaming_forward(qs, ks, vs, ST_INIT, ST_LOCAL, out=os_, rows=rw)
+            else:
+                e0 = Layer._ev(ev)
+                ops.dense_attention(qs, ks, vs, out=os_, rows=rw)
+            if ev is not None:
+                e1 = torch.cuda.Event(enable_timing=True)
+                e1.record()
+                ev.append((e0, e1))
+
+    def run(self, q=None, k=None, v=None, ev=None):
+        from minference.sharding import gather_row_ranges
+
+        q = self.q if q is None else q
+        k = self.k if k is None else k
+        v = self.v if v is None else v
+        first, second = self.halves[self.rank]
+        est = {}
+        self._run_pieces(first, est, q, k, v, ev)
+        main = torch.cuda.current_stream(self.device)
+        self.comm.wait_stream(main)
+        with torch.cuda.stream(self.comm):
+            gather_row_ranges(self.out, [h[0] for h in self.halves])
+        self._run_pieces(second, est, q, k, v, ev)
+        gather_row_ranges(self.out, [h[1] for h in self.halves])
+        main.wait_stream(self.comm)
+        return self.out
+
+    def launches_per_step(self) -> int:
+        n = 0
+        for half in self.halves[self.rank]:
+            for p, _s, _f, _r in self._batches(half):
+                n += {"vertical_and_slash": 3, "block_sparse": 2, "stream_llm": 1, "dense": 1}[p]
+        vs_b = {(b[1][0], len(b[1])) for half in self.halves[self.rank]
+                for b in self._batches(half) if b[0] in ("vertical_and_slash", "block_sparse")}
+        return n + 4 * len(vs_b)  # index estimation once per batch of heads
+
+    def visible_pairs(self) -> int:
+        ops, S, tot = self.ops, self.S, 0
+        for pc in self.parts[self.rank]:
+            i = self.local[pc.slot]
+            qs, ks = self.q[:, i:i + 1], self.k[:, i:i + 1]
+            p, rows = self.slot_pat[pc.slot], pc.rows(S)
+            if p == "vertical_and_slash":
+                vi, si = ops.vertical_and_slash_estimate(qs, ks, VS_V, VS_S)
+                tot += vs_visible_pairs(vi[0, 0], si[0, 0], S, rows)
+            elif p == "block_sparse":
+                idx = ops.select_block_sparse_topk_indices(qs, ks, BS_TOPK)
+                tot += bs_visible_pairs(idx[0, 0], S, rows)
+            elif p == "stream_llm":
+                tot += stream_visible_pairs(S, ST_INIT, ST_LOCAL, rows)
+            else:
+                r0, r1 = rows
+                tot += (r1 * (r1 + 1) - r0 * (r0 + 1)) // 2
         return tot
 
 
@@ -577,16 +706,24 @@ def time_reference_cpu(S: int, steps: int, warmup: int, layer=None):
     return dt / steps, fl / steps, layer
 
 
-def bench_config(args, S: int, world: int, split_gather: bool = False) -> dict:
+def bench_config(args, S: int, world: int) -> dict:
+    tiles = world > 1 and args.o_proj == "none" and args.partition == "tiles"
+    split_gather = world > 1 and args.o_proj == "none" and not tiles
+    if tiles:
+        par, gather, hmap = (f"tile-shard{world}",
+                             "row ranges exchanged point to point in two halves, the first "
+                             "overlapped with the remaining attention", "tiles")
+    else:
+        par = f"head-shard{world}" if world > 1 else "single"
+        gather = ("all-gather in two halves by local head, the first overlapped with the "
+                  "remaining attention" if split_gather else
+                  ("one all-gather" if world > 1 else "none"))
+        hmap = args.head_map if world > 1 else "single"
     return {"workload": "phi3-mini layer attention, mixed patterns (40% VS v=1000 s=6096, "
                         "40% block_sparse top-100, 20% stream 128+1024)",
             "model": "Phi-3-mini-128k attention shape", "global_batch": 1, "seq_len": S,
             "heads": args.heads, "head_dim": D, "pattern": args.pattern,
-            "parallelism": f"head-shard{world}" if world > 1 else "single",
-            "gather": ("all-gather in two halves by local head, the first overlapped "
-                       "with the remaining attention" if split_gather else
-                       ("one all-gather" if world > 1 else "none")),
-            "head_map": args.head_map if world > 1 else "single",
+            "parallelism": par, "gather": gather, "head_map": hmap,
             "o_proj": args.o_proj if world > 1 else "none",
             "l2": "inputs 1.2 GB > L2 (no flush needed)"}
 
@@ -835,7 +972,10 @@ def main():
                     help="N>1: follow the all-gather with Phi-3's o_proj GEMM, either after "
                          "the whole gather (serial) or chunk by chunk behind it (overlap)")
     ap.add_argument("--head-map", default="balanced", choices=["balanced", "contiguous"],
-                    help="head -> rank map for N>1 (minference.sharding)")
+                    help="head -> rank map for N>1 with --partition heads (minference.sharding)")
+    ap.add_argument("--partition", default="tiles", choices=["tiles", "heads"],
+                    help="N>1: split (head, query-tile) units of equal modelled cost over the "
+                         "ranks (tiles), or whole heads (heads)")
     ap.add_argument("--baseline-configs", action="store_true",
                     help="BASELINE configs 0-2 as single-layer ops (one JSON line each)")
     args = ap.parse_args()
@@ -875,9 +1015,13 @@ def main():
     # N>1, attention only: the layer output is all-gathered in two halves (by
     # local head), the first half as soon as its heads are done, overlapping
     # the attention of the rest.
-    split_gather = world > 1 and args.o_proj == "none"
-    layer = Layer(rank, world, S, device, args.pattern, args.heads, head_map,
-                  head_major_out=split_gather)
+    tiles = world > 1 and args.o_proj == "none" and args.partition == "tiles"
+    split_gather = world > 1 and args.o_proj == "none" and not tiles
+    if tiles:
+        layer = TileLayer(rank, world, S, device, args.pattern, args.heads)
+    else:
+        layer = Layer(rank, world, S, device, args.pattern, args.heads, head_map,
+                      head_major_out=split_gather)
     n_heads = args.heads
     gathered = None
     if world > 1 and not split_gather:
@@ -899,6 +1043,8 @@ def main():
         w_oproj = w.to(torch.bfloat16)[:, o_proj_input_permutation(head_map, D).to(device)]
 
     def step(q=None, k=None, v=None, ev=None):
+        if tiles:
+            return layer.run(q, k, v, ev)
         if split_gather:
             sent = []
 
@@ -1022,8 +1168,17 @@ def main():
     d1 = torch.cuda.Event(enable_timing=True)
     d_steps = max(1, min(args.steps, 3))
     d0.record()
+    # dense on this rank's head count (H / world heads)
+    n_loc = n_heads // world
+    sel = torch.arange(n_loc, device=device) % layer.q.shape[1]
+    dq_, dk2, dv2 = (layer.q.index_select(1, sel), layer.k.index_select(1, sel),
+                     layer.v.index_select(1, sel))
+    dout = torch.empty_like(dq_)
+    layer.ops.dense_attention(dq_, dk2, dv2, out=dout)
+    barrier()
+    d0.record()
     for _ in range(d_steps):
-        layer.ops.dense_attention(layer.q, layer.k, layer.v, out=layer.out)
+        layer.ops.dense_attention(dq_, dk2, dv2, out=dout)
     d1.record()
     barrier()
     dense_ms = max_over_ranks(d0.elapsed_time(d1) / d_steps)
@@ -1043,7 +1198,7 @@ def main():
                     d0.record()
                     for _ in range(d_steps):
                         torch.nn.functional.scaled_dot_product_attention(
-                            layer.q, layer.k, layer.v, is_causal=True, scale=D ** -0.5)
+                            dq_, dk2, dv2, is_causal=True, scale=D ** -0.5)
                     d1.record()
                     barrier()
                 sdpa_ms, sdpa_backend = max_over_ranks(d0.elapsed_time(d1) / d_steps), backend.name
@@ -1075,7 +1230,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1)/sqrt(96), rank-4 K bias, x4 sink keys)",
-            "config": bench_config(args, S, world, split_gather),
+            "config": bench_config(args, S, world),
             "ms_per_layer": ms,
             "dense_ms_per_layer": dense_ms,
             "sdpa_dense_ms_per_layer": sdpa_ms,

@@ -131,6 +131,19 @@ int mi_block_sparse_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor4 out
                         int64_t topk, float softmax_scale, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/* Row-window variant of mi_block_sparse_fwd: computes (and writes) only
+ * output rows [row_begin, row_end) -- whole 128-row tiles, except that the
+ * window may end at S -- with the same visible sets as the full call; other
+ * rows of `out` are left untouched.  q/k/v/out describe the whole sequence.
+ * Used to split one head's query tiles over several GPUs; the full call is
+ * the window [0, S).  No counterpart function in the reference (it serves
+ * the same op, block_sparse_kernel_npu.py:452-601, over part of the rows). */
+int mi_block_sparse_fwd_rows(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor4 out, int64_t B,
+                             int64_t H, int64_t S, int64_t D, int dtype, const int64_t* block_idx,
+                             int64_t topk, float softmax_scale, int64_t row_begin,
+                             int64_t row_end, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
 /* vertical_and_slash index estimation from the last min(64, S) queries:
  * v_idx int32 [B, H, vertical_size] ascending, s_idx int32 [B, H, slash_size]
  * descending (s = S-1-diagonal).  Columns 0..29 and slashes 0..99 are forced
@@ -158,6 +171,15 @@ int mi_vs_sparse_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor4 out, i
                      int64_t H, int64_t S, int64_t D, int dtype, const int32_t* v_idx,
                      int64_t nv, const int32_t* s_idx, int64_t ns, float softmax_scale,
                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* Row-window variant of mi_vs_sparse_fwd (window rules as in
+ * mi_block_sparse_fwd_rows).  No counterpart function in the reference (it
+ * serves vertical_slash_kernel_npu.py:255-415 over part of the rows). */
+int mi_vs_sparse_fwd_rows(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor4 out, int64_t B,
+                          int64_t H, int64_t S, int64_t D, int dtype, const int32_t* v_idx,
+                          int64_t nv, const int32_t* s_idx, int64_t ns, float softmax_scale,
+                          int64_t row_begin, int64_t row_end, void* workspace,
+                          size_t workspace_bytes, void* stream);
 
 /* Legacy four-array VS index format of upstream MInference, as restated by
  * the reference's CPU port convert_vertical_slash_indexes

@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int t = p.T - 1 - blockIdx.x;  // heavy (late) tiles first
+  const int t = p.t_lo + p.t_n - 1 - blockIdx.x;  // heavy (late) tiles first
   const int h = blockIdx.y;
   const int b = blockIdx.z;
   const int bh = b * p.H + h;
@@ -545,7 +545,7 @@ static int launch_attn_t(const mi_tensor4& q, const mi_tensor4& k, const mi_tens
   const int alloc = L::kAlloc;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, alloc);
   if (e == cudaSuccess) {
-    dim3 grid(prm.T, prm.H, prm.B);
+    dim3 grid(prm.t_n, prm.H, prm.B);
     kern<<<grid, kThreads, alloc, stream>>>(tq, tk, tv, to, prm);
     e = cudaGetLastError();
   }
@@ -564,7 +564,9 @@ int launch_attention(const mi_tensor4& q, const mi_tensor4& k, const mi_tensor4&
   prm.os_b = out.stride_b;
   prm.os_h = out.stride_h;
   prm.os_s = out.stride_s;
-  if (prm.T == 0 || prm.H == 0 || prm.B == 0) return MI_OK;
+  if (prm.t_n == 0 && prm.t_lo == 0) prm.t_n = prm.T;  // default: every tile
+  if (prm.t_lo < 0 || prm.t_n < 0 || prm.t_lo + prm.t_n > prm.T) return MI_ERR_SHAPE;
+  if (prm.t_n == 0 || prm.H == 0 || prm.B == 0) return MI_OK;
   const bool bf = dtype == MI_BF16;
   const bool split = prm.split != 0;
   if (split && prm.mode != 1) return MI_ERR_SHAPE;

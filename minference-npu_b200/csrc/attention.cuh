@@ -55,7 +55,8 @@ __host__ __device__ __forceinline__ int64_t plan_offset(int64_t t, int64_t cap) 
 struct AttnParams {
   int B, H, Sq, Sk;
   int q_off;           // Sk - Sq: absolute position of query row 0
-  int T;               // number of 128-row query tiles
+  int T;               // number of 128-row query tiles of the whole sequence
+  int t_lo, t_n;       // this launch computes tiles [t_lo, t_lo + t_n) (the whole range by default)
   int mode;            // 0: stream/dense arithmetic entries, 1: plan entries
   long long n_init;    // sink length (mode 0; 0 in mode 1)
   long long n_local;   // window length (mode 0; Sk+1 in mode 1)

@@ -383,16 +383,19 @@ extern "C" size_t mi_block_sparse_fwd_workspace_size(int64_t B, int64_t H, int64
   return align_up(sizeof(PlanEntry) * B * H * per_head) + align_up(sizeof(int) * B * H * T);
 }
 
-extern "C" int mi_block_sparse_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor4 out,
-                                   int64_t B, int64_t H, int64_t S, int64_t D, int dtype,
-                                   const int64_t* block_idx, int64_t topk, float softmax_scale,
-                                   void* workspace, size_t workspace_bytes, void* stream) {
+extern "C" int mi_block_sparse_fwd_rows(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v,
+                                        mi_tensor4 out, int64_t B, int64_t H, int64_t S,
+                                        int64_t D, int dtype, const int64_t* block_idx,
+                                        int64_t topk, float softmax_scale, int64_t row_begin,
+                                        int64_t row_end, void* workspace, size_t workspace_bytes,
+                                        void* stream) {
   if (dtype != MI_F16 && dtype != MI_BF16) return MI_ERR_DTYPE;
   if (B < 0 || H < 0 || S < 0 || topk < 1) return MI_ERR_SHAPE;
   if (D != 64 && D != 96 && D != 128) return MI_ERR_SHAPE;
   const int64_t nb = (S + 63) / 64, T = (S + 127) / 128;
   if (nb > kMaxBlocks || B > 65535 || H > 65535) return MI_ERR_SHAPE;
-  if (B == 0 || H == 0 || S == 0) return MI_OK;
+  if (!row_window_ok(row_begin, row_end, S)) return MI_ERR_SHAPE;
+  if (B == 0 || H == 0 || S == 0 || row_begin == row_end) return MI_OK;
   if (workspace_bytes < mi_block_sparse_fwd_workspace_size(B, H, S, topk) || !workspace)
     return MI_ERR_WORKSPACE;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -432,5 +435,15 @@ extern "C" int mi_block_sparse_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_
   prm.plan_cap = cap;
   prm.plan_head_stride = head_stride;
   prm.split = split ? 1 : 0;
+  prm.t_lo = (int)(row_begin / 128);
+  prm.t_n = (int)((row_end + 127) / 128) - prm.t_lo;
   return launch_attention(q, k, v, out, D, dtype, prm, st);
+}
+
+extern "C" int mi_block_sparse_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor4 out,
+                                   int64_t B, int64_t H, int64_t S, int64_t D, int dtype,
+                                   const int64_t* block_idx, int64_t topk, float softmax_scale,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+  return mi_block_sparse_fwd_rows(q, k, v, out, B, H, S, D, dtype, block_idx, topk, softmax_scale,
+                                  0, S, workspace, workspace_bytes, stream);
 }

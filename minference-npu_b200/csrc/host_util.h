@@ -13,6 +13,14 @@ namespace mib200 {
 
 inline size_t align_up(size_t x) { return (x + 255) & ~(size_t)255; }
 
+// A query-row window [row_begin, row_end) of an S-row sequence that the
+// attention launch can restrict itself to: whole 128-row tiles, except that
+// the window may end at S.
+inline bool row_window_ok(int64_t row_begin, int64_t row_end, int64_t S) {
+  if (row_begin < 0 || row_end < row_begin || row_end > S) return false;
+  return row_begin % 128 == 0 && (row_end % 128 == 0 || row_end == S);
+}
+
 // cuTensorMapEncodeTiled is fetched through the runtime's driver entry point
 // so the library does not link libcuda directly.
 inline PFN_cuTensorMapEncodeTiled_v12000 get_encode_tiled() {

@@ -573,16 +573,18 @@ extern "C" size_t mi_vs_sparse_fwd_workspace_size(int64_t B, int64_t H, int64_t 
   return vs_ws_layout(nullptr, B, H, S).bytes;
 }
 
-extern "C" int mi_vs_sparse_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor4 out,
-                                int64_t B, int64_t H, int64_t S, int64_t D, int dtype,
-                                const int32_t* v_idx, int64_t nv, const int32_t* s_idx,
-                                int64_t ns, float softmax_scale, void* workspace,
-                                size_t workspace_bytes, void* stream) {
+extern "C" int mi_vs_sparse_fwd_rows(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor4 out,
+                                     int64_t B, int64_t H, int64_t S, int64_t D, int dtype,
+                                     const int32_t* v_idx, int64_t nv, const int32_t* s_idx,
+                                     int64_t ns, float softmax_scale, int64_t row_begin,
+                                     int64_t row_end, void* workspace, size_t workspace_bytes,
+                                     void* stream) {
   if (dtype != MI_F16 && dtype != MI_BF16) return MI_ERR_DTYPE;
   if (D != 64 && D != 96 && D != 128) return MI_ERR_SHAPE;
   if (B < 0 || H < 0 || S < 0 || nv < 0 || ns < 0 || S > (1 << 24)) return MI_ERR_SHAPE;
   if (B > 65535 || H > 65535) return MI_ERR_SHAPE;
-  if (B == 0 || H == 0 || S == 0) return MI_OK;
+  if (!row_window_ok(row_begin, row_end, S)) return MI_ERR_SHAPE;
+  if (B == 0 || H == 0 || S == 0 || row_begin == row_end) return MI_OK;
   const VsWs w = vs_ws_layout(workspace, B, H, S);
   if (!workspace || workspace_bytes < w.bytes) return MI_ERR_WORKSPACE;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -610,7 +612,18 @@ extern "C" int mi_vs_sparse_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_ten
   prm.plan_count = w.count;
   prm.plan_cap = cap;
   prm.plan_head_stride = head_stride;
+  prm.t_lo = (int)(row_begin / 128);
+  prm.t_n = (int)((row_end + 127) / 128) - prm.t_lo;
   return launch_attention(q, k, v, out, D, dtype, prm, st);
+}
+
+extern "C" int mi_vs_sparse_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor4 out,
+                                int64_t B, int64_t H, int64_t S, int64_t D, int dtype,
+                                const int32_t* v_idx, int64_t nv, const int32_t* s_idx,
+                                int64_t ns, float softmax_scale, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  return mi_vs_sparse_fwd_rows(q, k, v, out, B, H, S, D, dtype, v_idx, nv, s_idx, ns,
+                               softmax_scale, 0, S, workspace, workspace_bytes, stream);
 }
 
 // ---------------------------------------------------------------------------

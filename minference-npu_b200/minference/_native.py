@@ -83,6 +83,9 @@ def lib() -> ctypes.CDLL:
         L.mi_block_sparse_fwd_workspace_size.restype = SZ
         L.mi_block_sparse_fwd.argtypes = [T4, T4, T4, T4, I64, I64, I64, I64, I, P, I64, F, P, SZ, P]
         L.mi_block_sparse_fwd.restype = I
+        L.mi_block_sparse_fwd_rows.argtypes = [T4, T4, T4, T4, I64, I64, I64, I64, I, P, I64, F,
+                                               I64, I64, P, SZ, P]
+        L.mi_block_sparse_fwd_rows.restype = I
         L.mi_vs_estimate_workspace_size.argtypes = [I64, I64, I64]
         L.mi_vs_estimate_workspace_size.restype = SZ
         L.mi_vs_estimate.argtypes = [T4, T4, I64, I64, I64, I64, I, I64, I64, F, P, P, P, SZ, P]
@@ -91,6 +94,9 @@ def lib() -> ctypes.CDLL:
         L.mi_vs_sparse_fwd_workspace_size.restype = SZ
         L.mi_vs_sparse_fwd.argtypes = [T4, T4, T4, T4, I64, I64, I64, I64, I, P, I64, P, I64, F, P, SZ, P]
         L.mi_vs_sparse_fwd.restype = I
+        L.mi_vs_sparse_fwd_rows.argtypes = [T4, T4, T4, T4, I64, I64, I64, I64, I, P, I64, P, I64,
+                                            F, I64, I64, P, SZ, P]
+        L.mi_vs_sparse_fwd_rows.restype = I
         L.mi_vs_convert_indexes.argtypes = [P, P, I64, P, I64, I64, I64, I64, P, P, P, P, P]
         L.mi_vs_convert_indexes.restype = I
         _lib = L

@@ -88,3 +88,15 @@ def output(out: torch.Tensor | None, shape: tuple, like: torch.Tensor) -> torch.
     if s[-1] != 1 or (s[0] * 2) % 16 or (s[1] * 2) % 16 or (s[2] * 2) % 16 or out.data_ptr() % 16:
         raise ValueError("out needs unit D stride and 16-byte aligned rows")
     return out
+
+
+def row_window(rows, S: int) -> tuple[int, int]:
+    """Validate an optional query-row window ``(row_begin, row_end)``: whole
+    128-row tiles, except that it may end at S.  None means every row."""
+    if rows is None:
+        return 0, S
+    r0, r1 = int(rows[0]), int(rows[1])
+    if not (0 <= r0 <= r1 <= S) or r0 % 128 or (r1 % 128 and r1 != S):
+        raise ValueError(f"rows={rows!r}: need 0 <= begin <= end <= S={S}, begin a multiple of "
+                         "128 and end a multiple of 128 or S")
+    return r0, r1

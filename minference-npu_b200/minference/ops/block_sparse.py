@@ -14,7 +14,8 @@ from __future__ import annotations
 import torch
 
 from .. import _native
-from ._common import check_qkv, default_softmax_scale, kernel_dim, prepare, reference_padded_dim
+from ._common import (check_qkv, default_softmax_scale, kernel_dim, prepare,
+                      reference_padded_dim, row_window)
 from ._common import output as _common_out
 
 __all__ = [
@@ -65,8 +66,12 @@ def select_block_sparse_topk_indices(q: torch.Tensor, k: torch.Tensor, topk_bloc
 def block_sparse_attention_from_indices(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                                         block_idx: torch.Tensor,
                                         softmax_scale: float | None = None, *,
-                                        out: torch.Tensor | None = None) -> torch.Tensor:
-    """Block-sparse causal attention over given key blocks ``[B,H,ceil(S/64),topk]``."""
+                                        out: torch.Tensor | None = None,
+                                        rows: tuple[int, int] | None = None) -> torch.Tensor:
+    """Block-sparse causal attention over given key blocks ``[B,H,ceil(S/64),topk]``.
+
+    ``rows=(begin, end)`` computes only those query rows (whole 128-row tiles,
+    the end may be S); the other rows of the output are left as they are."""
     check_qkv(q, k, v)
     B, H, S, D = q.shape
     if k.shape[2] != S:
@@ -77,24 +82,26 @@ def block_sparse_attention_from_indices(q: torch.Tensor, k: torch.Tensor, v: tor
     if idx.dim() != 4 or idx.shape[:3] != (B, H, -(-S // 64)):
         raise ValueError(f"block_idx must be [B,H,ceil(S/64),topk], got {tuple(idx.shape)}")
     topk = idx.shape[-1]
+    r0, r1 = row_window(rows, S)
     qp, kp, vp = prepare(q, dk), prepare(k, dk), prepare(v, dk)
     out = _common_out(out, (B, H, S, dk), q)
     ws = _native.workspace(_native.lib().mi_block_sparse_fwd_workspace_size(B, H, S, topk), q.device)
     with torch.cuda.device(q.device):
-        rc = _native.lib().mi_block_sparse_fwd(
+        rc = _native.lib().mi_block_sparse_fwd_rows(
             _native.t4(qp), _native.t4(kp), _native.t4(vp), _native.t4(out), B, H, S, dk,
-            _native.dtype_code(q), idx.data_ptr(), topk, scale, ws.data_ptr(), ws.numel(),
+            _native.dtype_code(q), idx.data_ptr(), topk, scale, r0, r1, ws.data_ptr(), ws.numel(),
             _native.stream_ptr(q.device),
         )
-    _native.check(rc, "mi_block_sparse_fwd")
+    _native.check(rc, "mi_block_sparse_fwd_rows")
     return out[..., :D] if dk != D else out
 
 
 def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, topk_blocks: int,
                            block_size: int = _DEFAULT_BLOCK_SIZE, *,
-                           out: torch.Tensor | None = None) -> torch.Tensor:
+                           out: torch.Tensor | None = None,
+                           rows: tuple[int, int] | None = None) -> torch.Tensor:
     """Block-sparse causal attention; same signature and semantics as the reference."""
     check_qkv(q, k, v)
     topk = max(1, int(topk_blocks))
     idx = select_block_sparse_topk_indices(q, k, topk, block_size)
-    return block_sparse_attention_from_indices(q, k, v, idx, out=out)
+    return block_sparse_attention_from_indices(q, k, v, idx, out=out, rows=rows)

@@ -18,7 +18,7 @@ import math
 import torch
 
 from .. import _native
-from ._common import check_qkv, default_softmax_scale, kernel_dim, prepare
+from ._common import check_qkv, default_softmax_scale, kernel_dim, prepare, row_window
 from ._common import output as _common_out
 
 __all__ = ["streaming_forward", "dense_attention"]
@@ -44,9 +44,27 @@ def _launch(q, k, v, n_init: int, n_local: int, scale: float,
     return out[..., :D] if dk != D else out
 
 
+def _window(q, k, v, out, rows):
+    """Restrict a causal problem to query rows [r0, r1): with bottom-right
+    alignment, rows r0.. of a full prefill are the last r1 - r0 rows of the
+    problem whose keys end at r1 (keys past a row are never visible)."""
+    S = q.shape[2]
+    if k.shape[2] != S:
+        raise NotImplementedError("rows= needs S_q == S_k (full prefill)")
+    r0, r1 = row_window(rows, S)
+    if out is None:
+        out = torch.zeros_like(q)
+    return q[:, :, r0:r1], k[:, :, :r1], v[:, :, :r1], out, out[:, :, r0:r1]
+
+
 def streaming_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_init: int,
-                      n_local: int, *, out: torch.Tensor | None = None) -> torch.Tensor:
+                      n_local: int, *, out: torch.Tensor | None = None,
+                      rows: tuple[int, int] | None = None) -> torch.Tensor:
     """Sink + sliding-window causal attention on BNSD ``[B,H,S,D]`` inputs.
+
+    ``rows=(begin, end)`` (full prefill only) computes only those query rows
+    (whole 128-row tiles, the end may be S); other output rows are left as
+    they are.
 
     Same signature and result as the reference.  The reference zero-pads D to
     the next supported head dim before anything else (streaming_kernel_npu.py:
@@ -57,6 +75,14 @@ def streaming_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_init:
     n_init = max(0, int(n_init))
     n_local = int(n_local)
     scale = default_softmax_scale(q.shape[-1])
+    if rows is not None:
+        qw, kw, vw, full, ow = _window(q, k, v, out, rows)
+        if qw.shape[2]:
+            if k.shape[2] <= n_local:  # the short-circuit is decided on the whole sequence
+                dense_attention(qw, kw, vw, scale=scale, causal=True, out=ow)
+            else:
+                _launch(qw, kw, vw, n_init, n_local, scale, ow)
+        return full
     if k.shape[2] <= n_local:
         return dense_attention(q, k, v, scale=scale, causal=True, out=out)
     return _launch(q, k, v, n_init, n_local, scale, out)
@@ -64,13 +90,21 @@ def streaming_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_init:
 
 def dense_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
                     scale: float | None = None, causal: bool = True,
-                    out: torch.Tensor | None = None) -> torch.Tensor:
+                    out: torch.Tensor | None = None,
+                    rows: tuple[int, int] | None = None) -> torch.Tensor:
     """Dense attention on BNSD ``[B,H,S,D]`` inputs (MInference-NPU
     minference/backend_npu/attention.py:192-211): ``scale`` defaults to
     ``1/sqrt(D)`` of the unpadded head dim; ``causal`` masks bottom-right
     aligned (row r sees keys ``j <= S_k - S_q + r``), otherwise every row sees
     every key.  Output has q's shape, dtype and device; ``out`` (optional) is a
     caller-owned ``[B,H,S_q,D]`` view written in place."""
+    if rows is not None:
+        if not causal:
+            raise NotImplementedError("rows= is for causal prefill")
+        qw, kw, vw, full, ow = _window(q, k, v, out, rows)
+        if qw.shape[2]:
+            dense_attention(qw, kw, vw, scale=scale, causal=True, out=ow)
+        return full
     check_qkv(q, k, v)
     B, H, S_q, D = q.shape
     S_k = k.shape[2]

@@ -15,7 +15,7 @@ import math
 import torch
 
 from .. import _native
-from ._common import check_qkv, default_softmax_scale, kernel_dim, prepare
+from ._common import check_qkv, default_softmax_scale, kernel_dim, prepare, row_window
 from ._common import output as _common_out
 
 __all__ = [
@@ -55,8 +55,12 @@ def vertical_slash_sparse_attention(query: torch.Tensor, key: torch.Tensor, valu
                                     v_idx: torch.Tensor, s_idx: torch.Tensor,
                                     block_size_M: int = 64, block_size_N: int = 64,
                                     softmax_scale: float | None = None, *,
-                                    out: torch.Tensor | None = None) -> torch.Tensor:
-    """Vertical-slash causal attention; same signature as the reference op."""
+                                    out: torch.Tensor | None = None,
+                                    rows: tuple[int, int] | None = None) -> torch.Tensor:
+    """Vertical-slash causal attention; same signature as the reference op.
+
+    ``rows=(begin, end)`` computes only those query rows (whole 128-row tiles,
+    the end may be S); the other rows of the output are left as they are."""
     check_qkv(query, key, value)
     if block_size_M != 64 or block_size_N != 64:
         raise NotImplementedError("block_size_M/N must be 64")
@@ -66,6 +70,7 @@ def vertical_slash_sparse_attention(query: torch.Tensor, key: torch.Tensor, valu
         f"got S_q={S}, S_k={key.shape[2]}"
     )
     scale = default_softmax_scale(D) if softmax_scale is None else float(softmax_scale)
+    r0, r1 = row_window(rows, S)
     dk = kernel_dim(D)
     vi = v_idx.to(device=query.device, dtype=torch.int32).reshape(B, H, -1).contiguous()
     si = s_idx.to(device=query.device, dtype=torch.int32).reshape(B, H, -1).contiguous()
@@ -73,20 +78,21 @@ def vertical_slash_sparse_attention(query: torch.Tensor, key: torch.Tensor, valu
     out = _common_out(out, (B, H, S, dk), query)
     ws = _native.workspace(_native.lib().mi_vs_sparse_fwd_workspace_size(B, H, S), query.device)
     with torch.cuda.device(query.device):
-        rc = _native.lib().mi_vs_sparse_fwd(
+        rc = _native.lib().mi_vs_sparse_fwd_rows(
             _native.t4(qp), _native.t4(kp), _native.t4(vp), _native.t4(out), B, H, S, dk,
             _native.dtype_code(query), vi.data_ptr(), vi.shape[-1], si.data_ptr(), si.shape[-1],
-            scale, ws.data_ptr(), ws.numel(), _native.stream_ptr(query.device),
+            scale, r0, r1, ws.data_ptr(), ws.numel(), _native.stream_ptr(query.device),
         )
-    _native.check(rc, "mi_vs_sparse_fwd")
+    _native.check(rc, "mi_vs_sparse_fwd_rows")
     return out[..., :D] if dk != D else out
 
 
 def vertical_and_slash(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, vertical_size: int,
-                       slash_size: int, *, out: torch.Tensor | None = None) -> torch.Tensor:
+                       slash_size: int, *, out: torch.Tensor | None = None,
+                       rows: tuple[int, int] | None = None) -> torch.Tensor:
     """Estimate indices from the last 64 queries, then run the sparse attention."""
     v_idx, s_idx = vertical_and_slash_estimate(q, k, vertical_size, slash_size)
-    return vertical_slash_sparse_attention(q, k, v, v_idx, s_idx, out=out)
+    return vertical_slash_sparse_attention(q, k, v, v_idx, s_idx, out=out, rows=rows)
 
 
 def convert_vertical_slash_indexes(seqlens: torch.Tensor, vertical_indexes: torch.Tensor,

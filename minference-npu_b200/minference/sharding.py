@@ -13,6 +13,14 @@ Two head maps:
     with equal head counts per rank, so the layer time (set by the slowest
     rank) drops when the pattern mix is uneven across contiguous ranges.
     `gather_heads_mapped` re-assembles head order after the all-gather.
+
+Heads differ in cost by ~30x between patterns, so whole heads cannot always
+balance (13 vertical_and_slash heads over 8 ranks leave some rank with two).
+Query tiles are independent in every pattern too, so `tile_partition` cuts
+the layer's (head, 128-row tile) units into contiguous per-rank ranges of
+equal modelled cost; a rank then runs row windows (``rows=``) of a few heads,
+and `gather_row_ranges` re-assembles the ``[B, H, S, D]`` output, in which
+each rank's range is one contiguous block of memory.
 """
 
 from __future__ import annotations
@@ -21,7 +29,8 @@ import torch
 import torch.distributed as dist
 
 __all__ = ["head_range", "gather_heads", "head_cost", "balanced_head_map",
-           "gather_heads_mapped", "o_proj_input_permutation", "gather_o_proj"]
+           "gather_heads_mapped", "o_proj_input_permutation", "gather_o_proj",
+           "tile_costs", "tile_partition", "Piece", "unit_range_split", "gather_row_ranges"]
 
 
 def head_range(num_heads: int, rank: int, world: int) -> range:
@@ -218,4 +227,151 @@ def gather_o_proj(local_bshd: torch.Tensor, weight_perm: torch.Tensor, bias=None
         main.wait_event(events[c])
         project(bufs[c].unbind(0), bounds[c], bounds[c + 1])
     x.record_stream(comm)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# (head, query-tile) partition
+# ---------------------------------------------------------------------------
+TILE_ROWS = 128
+# fixed cost of one 128-row tile (setup, Q load, epilogue) in units of one
+# 64-key block step of the attention kernel
+TILE_OVERHEAD = 4.0
+
+
+def tile_costs(pattern, S: int) -> list[float]:
+    """Modelled cost of each 128-row query tile of one head: the 64-key
+    blocks the attention kernel walks for it, plus a fixed per-tile cost.
+
+    vertical_and_slash and dense walk the causal blocks (2t + 2 for tile t;
+    at long contexts the VS set covers nearly all of them); block_sparse
+    walks max over its two query blocks of min(top-k, causal blocks);
+    stream_llm walks its sink and window blocks."""
+    ty = pattern[0]
+    T = -(-S // TILE_ROWS)
+    out = []
+    for t in range(T):
+        causal = 2 * t + 2
+        if ty in ("vertical_and_slash", "dense"):
+            n = causal
+        elif ty == "block_sparse":
+            n = min(max(1, int(pattern[1])), causal)
+        elif ty == "stream_llm":
+            n_init, n_local = int(pattern[1]), int(pattern[2])
+            n = min(causal, -(-n_init // 64) + -(-(n_local + TILE_ROWS) // 64) + 1)
+        else:
+            raise ValueError(f"unknown pattern type {ty!r}")
+        out.append(n + TILE_OVERHEAD)
+    return out
+
+
+class Piece(tuple):
+    """(slot, t0, t1): query tiles [t0, t1) of the head stored at position
+    `slot` of the layer's head order (rows [128*t0, min(128*t1, S)))."""
+
+    __slots__ = ()
+
+    def __new__(cls, slot: int, t0: int, t1: int):
+        return tuple.__new__(cls, (slot, t0, t1))
+
+    slot = property(lambda self: self[0])
+    t0 = property(lambda self: self[1])
+    t1 = property(lambda self: self[2])
+
+    def rows(self, S: int) -> tuple[int, int]:
+        return self.t0 * TILE_ROWS, min(self.t1 * TILE_ROWS, S)
+
+
+def tile_partition(patterns, S: int, world: int) -> list[list[Piece]]:
+    """Split the layer into `world` contiguous ranges of (head, tile) units.
+
+    Units are ordered head by head (in the order of `patterns`, one pattern
+    tuple per head slot) and tile by tile inside a head, which is the memory
+    order of a contiguous ``[1, H, S, D]`` output, so each rank's range is
+    one contiguous block of it.  Rank r takes the units whose cost prefix
+    midpoint falls in [r, r+1) * total / world.  Returns, per rank, its
+    pieces in unit order."""
+    if world <= 0:
+        raise ValueError(f"bad world size {world}")
+    costs = [tile_costs(p, S) for p in patterns]
+    total = sum(sum(c) for c in costs)
+    parts: list[list[Piece]] = [[] for _ in range(world)]
+    acc = 0.0
+    for slot, cs in enumerate(costs):
+        cur_r, t_start = None, 0
+        for t, c in enumerate(cs):
+            r = min(world - 1, int((acc + c / 2) * world / total)) if total > 0 else 0
+            acc += c
+            if r != cur_r:
+                if cur_r is not None:
+                    parts[cur_r].append(Piece(slot, t_start, t))
+                cur_r, t_start = r, t
+        if cur_r is not None:
+            parts[cur_r].append(Piece(slot, t_start, len(cs)))
+    return parts
+
+
+def unit_range_split(pieces: list[Piece], patterns, S: int, frac: float = 0.5):
+    """Cut one rank's pieces (in unit order) where `frac` of their modelled
+    cost is reached: returns (first, second) piece lists, a piece straddling
+    the cut being split at a tile boundary."""
+    costs = [tile_costs(patterns[p.slot], S) for p in pieces]
+    total = sum(sum(c[p.t0:p.t1]) for p, c in zip(pieces, costs))
+    target = frac * total
+    first, second, acc = [], [], 0.0
+    for p, c in zip(pieces, costs):
+        if acc >= target:
+            second.append(p)
+            continue
+        cut = p.t1
+        for t in range(p.t0, p.t1):
+            if acc >= target:
+                cut = t
+                break
+            acc += c[t]
+        if cut > p.t0:
+            first.append(Piece(p.slot, p.t0, cut))
+        if cut < p.t1:
+            second.append(Piece(p.slot, cut, p.t1))
+    return first, second
+
+
+def _flat_span(pieces: list[Piece], S: int, D: int) -> tuple[int, int] | None:
+    """Element span [lo, hi) of contiguous unit-ordered pieces inside a
+    contiguous [1, H, S, D] buffer."""
+    if not pieces:
+        return None
+    a, b = pieces[0], pieces[-1]
+    lo = (a.slot * S + a.rows(S)[0]) * D
+    hi = (b.slot * S + b.rows(S)[1]) * D
+    return lo, hi
+
+
+def gather_row_ranges(out: torch.Tensor, pieces_per_rank: list[list[Piece]], group=None):
+    """In-place all-gather of row ranges: `out` is a contiguous ``[1, H, S, D]``
+    tensor in which this rank has computed its pieces; afterwards every rank
+    holds every rank's pieces.  Each rank's pieces must form one contiguous
+    unit range (as `tile_partition` and `unit_range_split` produce).  The
+    exchange is one batch of point-to-point sends and receives (NCCL groups
+    them; gloo runs them as plain sends)."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    if out.dim() != 4 or out.shape[0] != 1 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous [1, H, S, D] tensor")
+    _, H, S, D = out.shape
+    flat = out.view(-1)
+    spans = [_flat_span(p, S, D) for p in pieces_per_rank]
+    ops = []
+    mine = spans[rank]
+    for peer in range(world):
+        if peer == rank:
+            continue
+        if mine is not None:
+            ops.append(dist.P2POp(dist.isend, flat[mine[0]:mine[1]], peer, group))
+        if spans[peer] is not None:
+            lo, hi = spans[peer]
+            ops.append(dist.P2POp(dist.irecv, flat[lo:hi], peer, group))
+    if ops:
+        for w in dist.batch_isend_irecv(ops):
+            w.wait()
     return out

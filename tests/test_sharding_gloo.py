@@ -183,3 +183,93 @@ def test_gather_o_proj_gloo():
     for p in procs:
         p.join(timeout=60)
     assert all(ok for _, ok, _ in res), res
+
+
+CYCLE = [("vertical_and_slash", 1000, 6096), ("block_sparse", 100, 0),
+         ("vertical_and_slash", 1000, 6096), ("block_sparse", 100, 0), ("stream_llm", 128, 1024)]
+
+
+def _mixed_layout(n=32):
+    pats = [CYCLE[h % 5] for h in range(n)]
+    order = ("stream_llm", "block_sparse", "vertical_and_slash")
+    return [pats[h] for h in sorted(range(n), key=lambda h: (order.index(pats[h][0]), h))]
+
+
+def test_tile_partition_covers_and_balances():
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "minference-npu_b200"))
+    from minference.sharding import (balanced_head_map, head_cost, tile_costs, tile_partition,
+                                     unit_range_split)
+
+    S = 65536
+    pats = _mixed_layout()
+    T = S // 128
+    for world in (1, 2, 3, 4, 8):
+        parts = tile_partition(pats, S, world)
+        units = [(pc.slot, t) for pr in parts for pc in pr for t in range(pc.t0, pc.t1)]
+        assert units == [(h, t) for h in range(32) for t in range(T)]  # contiguous, in order
+        loads = [sum(sum(tile_costs(pats[pc.slot], S)[pc.t0:pc.t1]) for pc in pr) for pr in parts]
+        assert max(loads) <= 1.01 * sum(loads) / world
+        for pr in parts:
+            a, b = unit_range_split(pr, pats, S)
+            assert [(pc.slot, t) for pc in a + b for t in range(pc.t0, pc.t1)] == \
+                [(pc.slot, t) for pc in pr for t in range(pc.t0, pc.t1)]
+    # at 8 ranks whole heads cannot balance the 13 VS heads; tiles can
+    costs = [head_cost(p, S) for p in pats]
+    m8 = balanced_head_map(costs, 8)
+    heads_max = max(sum(costs[h] for h in hs) for hs in m8) / (sum(costs) / 8)
+    assert heads_max > 1.1
+
+
+def _worker_rows(rank, world, port, S, q):
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "minference-npu_b200"))
+    import torch.distributed as dist
+
+    from minference.sharding import gather_row_ranges, tile_partition, unit_range_split
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        pats = _mixed_layout(10)
+        H, D = len(pats), 4
+        g = torch.Generator().manual_seed(5)
+        want = torch.randn(1, H, S, D, generator=g)
+        parts = tile_partition(pats, S, world)
+        halves = [unit_range_split(pr, pats, S) for pr in parts]
+        out = torch.zeros_like(want)
+        ok = True
+        for phase in (0, 1):
+            for pc in halves[rank][phase]:  # "compute" this rank's rows
+                r0, r1 = pc.rows(S)
+                out[:, pc.slot, r0:r1] = want[:, pc.slot, r0:r1]
+            gather_row_ranges(out, [h[phase] for h in halves])
+            if phase == 0:  # after phase 0 every rank holds every first half
+                for h in halves:
+                    for pc in h[0]:
+                        r0, r1 = pc.rows(S)
+                        ok &= torch.equal(out[:, pc.slot, r0:r1], want[:, pc.slot, r0:r1])
+        q.put((rank, bool(ok and torch.equal(out, want)), None))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,S", [(2, 1024), (3, 1000)])
+def test_gather_row_ranges_gloo(world, S):
+    """Each rank fills its (head, tile) pieces; the two-phase row-range
+    exchange leaves every rank with the whole [1, H, S, D] output."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_rows, args=(r, world, port, S, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(ok for _, ok, _ in res), res
