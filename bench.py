@@ -52,6 +52,7 @@ def dense_causal_flops(S: int, H: int, d: int = D) -> float:
 
 
 PATTERN_KEYS = {"vertical_and_slash": ("vertical_and_slash", VS_V, VS_S),
+                "vs_local": ("vertical_and_slash", VS_V, VS_S),
                 "block_sparse": ("block_sparse", BS_TOPK, 0),
                 "stream_llm": ("stream_llm", ST_INIT, ST_LOCAL), "dense": ("dense", 0, 0)}
 
@@ -77,7 +78,7 @@ def shard_groups(rank: int, world: int, pattern: str = "mixed", n_heads: int = H
     groups = []
     # cheapest groups first: with N>1 the first half of the heads (the first
     # all-gather) is then ready early and its transfer hides behind the rest
-    for p in ("stream_llm", "block_sparse", "vertical_and_slash", "dense"):
+    for p in ("stream_llm", "block_sparse", "vertical_and_slash", "vs_local", "dense"):
         hs = [h for h in heads if pats[h] == p]
         if hs:
             groups.append((p, hs))
@@ -162,6 +163,50 @@ def vs_visible_pairs(v_idx: torch.Tensor, s_idx: torch.Tensor, S: int, rows=None
         # key j in the diagonal block is seen by rows i >= j: 64 - (j - start) rows
         total += (ind * (64 - (j - start))).sum().item()
     return int(total)
+
+
+def vs_plan_steps(v_idx: torch.Tensor, s_idx: torch.Tensor, S: int, gather: bool = True) -> int:
+    """64-key steps the attention kernel issues for one VS head (S % 128 == 0):
+    per 128-row tile, the key blocks a slash reaches for either of its two
+    query blocks (or that hold a vertical column at or after the first query
+    block), plus, with gathering, one step per 64 gathered columns (vertical
+    columns of blocks no slash reaches, before both query blocks); without
+    gathering every block holding a vertical column is a step."""
+    dev = v_idx.device
+    nb = S // 64
+    s = s_idx.long()
+    vert = torch.zeros(S, dtype=torch.bool, device=dev)
+    vert[v_idx.long().clamp(0, S - 1)] = True
+    vblk = vert.view(nb, 64)
+    total = 0
+    for c0 in range(0, nb, 256):
+        bq = torch.arange(c0, min(nb, c0 + 256), device=dev)
+        end_m = (bq + 1) * 64
+        valid = s[None, :] < end_m[:, None]
+        re = (end_m[:, None] - s[None, :]).clamp(min=64).clamp(max=S)
+        rs = (re - 64).clamp(min=0)
+        delta = torch.zeros(len(bq), S + 1, dtype=torch.int32, device=dev)
+        ones = valid.to(torch.int32)
+        delta.scatter_add_(1, torch.where(valid, rs, S), ones)
+        delta.scatter_add_(1, torch.where(valid, re, S), -ones)
+        cov = (delta.cumsum(1)[:, :S] > 0).view(len(bq), nb, 64)
+        kb = torch.arange(nb, device=dev)[None, :]
+        causal = kb <= bq[:, None]
+        slash_blk = cov.any(-1) & causal                      # [n, nb]
+        vert_blk = vblk.any(-1)[None, :] & causal
+        # pair query blocks into tiles (c0 is even)
+        sb = slash_blk.view(-1, 2, nb).any(1)
+        vb = vert_blk.view(-1, 2, nb).any(1)
+        bq0 = bq.view(-1, 2)[:, 0:1]
+        if gather:
+            gath = vb & ~sb & (kb < bq0)
+            steps = (sb | (vb & ~gath)).sum(1)
+            ncols = (vblk[None, :, :] & gath[:, :, None]).sum((1, 2))
+            steps = steps + (ncols + 63) // 64
+        else:
+            steps = (sb | vb).sum(1)
+        total += int(steps.sum().item())
+    return total
 
 
 # ---------------------------------------------------------------------------
@@ -268,6 +313,8 @@ class Layer:
         for p, hs in self.groups:
             self.slices.append((p, slice(h0, h0 + len(hs))))
             h0 += len(hs)
+        self.local_vs = (local_vs_indices(len(self.heads), S, device)
+                         if any(p == "vs_local" for p, _ in self.groups) else None)
         # the same groups as (pattern key, local heads), the dispatcher's format
         self.run_spec = [(PATTERN_KEYS[p], list(range(sl.start, sl.stop))) for p, sl in self.slices]
 
@@ -293,6 +340,10 @@ class Layer:
             elif p == "stream_llm":
                 a = self._ev(ev)
                 ops.streaming_forward(qs, ks, vs, ST_INIT, ST_LOCAL, out=os_)
+            elif p == "vs_local":
+                a = self._ev(ev)
+                ops.vertical_slash_sparse_attention(qs, ks, vs, self.local_vs[0][:, sl],
+                                                    self.local_vs[1][:, sl], out=os_)
             else:
                 a = self._ev(ev)
                 ops.dense_attention(qs, ks, vs, out=os_)
@@ -315,7 +366,8 @@ class Layer:
     def launches_per_step(self) -> int:
         n = 0
         for p, _ in self.slices:
-            n += {"vertical_and_slash": 4 + 3, "block_sparse": 2 + 2, "stream_llm": 1, "dense": 1}[p]
+            n += {"vertical_and_slash": 4 + 3, "vs_local": 3, "block_sparse": 2 + 2,
+                  "stream_llm": 1, "dense": 1}[p]
         return n
 
     def visible_pairs(self) -> int:
@@ -333,9 +385,41 @@ class Layer:
                     tot += bs_visible_pairs(idx[0, h], self.S)
             elif p == "stream_llm":
                 tot += stream_visible_pairs(self.S, ST_INIT, ST_LOCAL) * (sl.stop - sl.start)
+            elif p == "vs_local":
+                vi, si = self.local_vs
+                for h in range(sl.start, sl.stop):
+                    tot += vs_visible_pairs(vi[0, h], si[0, h], self.S)
             else:
                 tot += self.S * (self.S + 1) // 2 * (sl.stop - sl.start)
         return tot
+
+    def vs_local_stats(self) -> dict:
+        """Structured VS heads: issued 64-key steps with and without gathered
+        columns against the algorithmic visible pairs (in 128 x 64 steps)."""
+        vi, si = self.local_vs
+        vis = g_on = g_off = 0
+        for h in range(vi.shape[1]):
+            vis += vs_visible_pairs(vi[0, h], si[0, h], self.S)
+            g_on += vs_plan_steps(vi[0, h], si[0, h], self.S, True)
+            g_off += vs_plan_steps(vi[0, h], si[0, h], self.S, False)
+        alg = vis / (128 * 64)
+        return {"visible_fraction": vis / (vi.shape[1] * self.S * (self.S + 1) / 2),
+                "steps_gathered": g_on, "steps_blocks_only": g_off,
+                "tensor_work_over_algorithmic": g_on / alg,
+                "tensor_work_over_algorithmic_blocks_only": g_off / alg}
+
+
+def local_vs_indices(n_heads: int, S: int, device):
+    """Structured vertical_and_slash index sets as real configs have them:
+    the VS_S nearest diagonals (local slashes, 0..VS_S-1) and VS_V vertical
+    columns, the 30 the estimator forces plus seeded scattered ones."""
+    vis, sis = [], []
+    for h in range(n_heads):
+        g = torch.Generator().manual_seed(500 + h)
+        cols = torch.cat([torch.arange(30), 30 + torch.randperm(S - 30, generator=g)[:VS_V - 30]])
+        vis.append(cols.sort().values)
+        sis.append(torch.arange(VS_S - 1, -1, -1))
+    return (torch.stack(vis)[None].int().to(device), torch.stack(sis)[None].int().to(device))
 
 
 class TileLayer:
@@ -957,7 +1041,8 @@ def main():
     ap.add_argument("--seq", type=int, default=SEQ)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pattern", default="mixed",
-                    choices=["mixed", "vertical_and_slash", "block_sparse", "stream_llm", "dense"],
+                    choices=["mixed", "vertical_and_slash", "block_sparse", "stream_llm", "dense",
+                             "vs_local"],
                     help="all heads use one pattern (profiling / per-pattern numbers)")
     ap.add_argument("--heads", type=int, default=H_TOTAL)
     ap.add_argument("--ttft", action="store_true",
@@ -1249,6 +1334,7 @@ def main():
                          "kernel": "attn_fwd_kernel (+ plan kernels), visible-pair FLOPs 4*D*N_vis",
                          "visible_fraction": vis_pairs / (len(layer.heads) * S * (S + 1) / 2)},
             "clocks": clk,
+            **({"vs_local": layer.vs_local_stats()} if args.pattern == "vs_local" else {}),
             "e2e": {"value": dense_flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
                     "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world, "mode": e2e_mode},

@@ -1,6 +1,8 @@
 // Sparse FlashAttention forward kernel (tcgen05 + TMA) and its host launcher.
 // Design notes are at the top of attention.cuh.
 #include "attention.cuh"
+#include <cstring>
+
 #include "host_util.h"
 
 namespace mib200 {
@@ -49,12 +51,14 @@ __device__ __forceinline__ int split_row(int L) {
   return ((L & 31) < 16) ? (L >> 5) * 16 + (L & 15) : 64 + (L >> 5) * 16 + (L & 15);
 }
 
-template <typename DT, int D, bool SPLIT>
+template <typename DT, int D, bool SPLIT, bool GATHER>
 __global__ void __launch_bounds__(kThreads, 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v,
-                    const __grid_constant__ CUtensorMap tm_o, const AttnParams p) {
+                    const __grid_constant__ CUtensorMap tm_o,
+                    const __grid_constant__ CUtensorMap tm_kr,
+                    const __grid_constant__ CUtensorMap tm_vr, const AttnParams p) {
   using L = AttnSmem<D, SPLIT>;
   constexpr int NC = L::NC;
   constexpr int KS = L::KS, VS = L::VS;
@@ -94,6 +98,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   // ---- entry list of this tile -------------------------------------------
   EntrySource src;
   src.mode = p.mode;
+  const int32_t* gcols = nullptr;  // gathered key positions of this tile
   int n_entries;
   if (p.mode == 0) {
     const long long a_lo = (long long)p.q_off + (long long)t * kBM;
@@ -117,6 +122,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     src.band_start = 0;
     src.list = p.plan + (long long)bh * p.plan_head_stride + plan_offset(t, p.plan_cap);
     n_entries = p.plan_count[(long long)bh * p.T + t];
+    if (GATHER) gcols = p.gcols + ((long long)bh * p.T + t) * p.gmax * 64;
   }
 
   // ---- one-time setup -------------------------------------------------------
@@ -169,11 +175,29 @@ __global__ void __launch_bounds__(kThreads, 2)
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
+      if (GATHER) {
+        tma_prefetch_desc(&tm_kr);
+        tma_prefetch_desc(&tm_vr);
+      }
       mbar_arrive_expect_tx(q_full, L::kQBytes);
       for (int c = 0; c < NC; ++c)
         tma_load_4d(smem + L::kQOff + c * (kBM * 64), &tm_q, q_full, c * 32, t * kBM, h, b);
       // A stage holds one key block per entry, or two in a split tile
       // (the block of query rows [0,64), then the block of rows [64,128)).
+      // A gathered group (kb < 0; GATHER kernels only) loads its up to 64 key
+      // rows four at a time through the 2-D row view; empty slots load key 0
+      // of the head, which the group's masks leave invisible.
+      const long long row0 = (long long)b * p.grow_b + (long long)h * p.grow_h;
+      auto gather_rows = [&](uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int g) {
+        const int4* cols = reinterpret_cast<const int4*>(gcols + g * 64);
+        for (int rg = 0; rg < kBN / 4; ++rg) {
+          const int4 c = cols[rg];
+          const int r0 = (int)(row0 + max(c.x, 0)), r1 = (int)(row0 + max(c.y, 0));
+          const int r2 = (int)(row0 + max(c.z, 0)), r3 = (int)(row0 + max(c.w, 0));
+          for (int cc = 0; cc < NC; ++cc)
+            tma_gather4_2d(dst + cc * (kBN * 64) + rg * 256, map, bar, cc * 32, r0, r1, r2, r3);
+        }
+      };
       auto load_k = [&](int j) -> bool {
         const int st = j % KS, use = j / KS;
         if (use > 0 && !mbar_wait(&k_empty[st], (use - 1) & 1, 101)) return false;
@@ -182,6 +206,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         src.get(j, kb[0], kb[1], m0, m1);
         uint8_t* dst = smem + L::kKOff + st * L::kKStage;
         mbar_arrive_expect_tx(&k_full[st], L::kKStage);
+        if (GATHER && kb[0] < 0) {
+          gather_rows(dst, &tm_kr, &k_full[st], -1 - kb[0]);
+          return true;
+        }
         for (int hb = 0; hb < L::NB; ++hb)
           for (int c = 0; c < NC; ++c)
             tma_load_4d(dst + hb * L::kKVBytes + c * (kBN * 64), &tm_k, &k_full[st], c * 32,
@@ -196,6 +224,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         src.get(j, kb[0], kb[1], m0, m1);
         uint8_t* dst = smem + L::kVOff + st * L::kVStage;
         mbar_arrive_expect_tx(&v_full[st], L::NB * L::kKVBytes);
+        if (GATHER && kb[0] < 0) {
+          gather_rows(dst, &tm_vr, &v_full[st], -1 - kb[0]);
+          return true;
+        }
         for (int hb = 0; hb < L::NB; ++hb)
           for (int c = 0; c < NC; ++c)
             tma_load_4d(dst + hb * L::kVBytes + c * (kBN * 64), &tm_v, &v_full[st], c * 32,
@@ -354,6 +386,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc_fence_after();
       MI_TR(1, j);
 
+      // A gathered group has kb < 0, so key0 <= -64: with n_init = 0 and the
+      // unbounded n_local of mode 1 every positional term below is all ones
+      // and its visibility is its mask alone.
       const long long key0 = (long long)kb * kBN;
       // Visible keys of this row inside the block:
       //   mask AND key <= a AND key < Sk AND (key < n_init OR key > a - n_local).
@@ -531,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 // ---------------------------------------------------------------------------
 // Host launcher
 // ---------------------------------------------------------------------------
-template <typename DT, int D, bool SPLIT>
+template <typename DT, int D, bool SPLIT, bool GATHER>
 static int launch_attn_t(const mi_tensor4& q, const mi_tensor4& k, const mi_tensor4& v,
                          const mi_tensor4& out, AttnParams prm, cudaStream_t stream) {
   using L = AttnSmem<D, SPLIT>;
@@ -541,12 +576,21 @@ static int launch_attn_t(const mi_tensor4& q, const mi_tensor4& k, const mi_tens
   if ((rc = make_bnsd_map(&tk, k, prm.B, prm.H, prm.Sk, D, 32, kBN)) != MI_OK) return rc;
   if ((rc = make_bnsd_map(&tv, v, prm.B, prm.H, prm.Sk, D, 32, kBN)) != MI_OK) return rc;
   if ((rc = make_bnsd_map(&to, out, prm.B, prm.H, prm.Sq, D, 32, kBM)) != MI_OK) return rc;
-  auto kern = attn_fwd_kernel<DT, D, SPLIT>;
+  CUtensorMap tkr, tvr;  // 2-D row views of K and V (gathered groups only)
+  memset(&tkr, 0, sizeof(tkr));
+  memset(&tvr, 0, sizeof(tvr));
+  if (GATHER) {
+    const long long rows = (long long)(prm.B - 1) * prm.grow_b + (long long)(prm.H - 1) * prm.grow_h +
+                           prm.Sk;
+    if ((rc = make_rows_map(&tkr, k.ptr, rows, k.stride_s, D, 32)) != MI_OK) return rc;
+    if ((rc = make_rows_map(&tvr, v.ptr, rows, v.stride_s, D, 32)) != MI_OK) return rc;
+  }
+  auto kern = attn_fwd_kernel<DT, D, SPLIT, GATHER>;
   const int alloc = L::kAlloc;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, alloc);
   if (e == cudaSuccess) {
     dim3 grid(prm.t_n, prm.H, prm.B);
-    kern<<<grid, kThreads, alloc, stream>>>(tq, tk, tv, to, prm);
+    kern<<<grid, kThreads, alloc, stream>>>(tq, tk, tv, to, tkr, tvr, prm);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) {
@@ -570,13 +614,18 @@ int launch_attention(const mi_tensor4& q, const mi_tensor4& k, const mi_tensor4&
   const bool bf = dtype == MI_BF16;
   const bool split = prm.split != 0;
   if (split && prm.mode != 1) return MI_ERR_SHAPE;
+  const bool gather = prm.gather != 0;
+  if (gather && (split || prm.mode != 1)) return MI_ERR_SHAPE;
 #define MI_ATTN_CASE(DD)                                                                  \
   if (D == DD) {                                                                         \
     if (split)                                                                           \
-      return bf ? launch_attn_t<__nv_bfloat16, DD, true>(q, k, v, out, prm, stream)      \
-                : launch_attn_t<__half, DD, true>(q, k, v, out, prm, stream);            \
-    return bf ? launch_attn_t<__nv_bfloat16, DD, false>(q, k, v, out, prm, stream)       \
-              : launch_attn_t<__half, DD, false>(q, k, v, out, prm, stream);             \
+      return bf ? launch_attn_t<__nv_bfloat16, DD, true, false>(q, k, v, out, prm, stream) \
+                : launch_attn_t<__half, DD, true, false>(q, k, v, out, prm, stream);      \
+    if (gather)                                                                          \
+      return bf ? launch_attn_t<__nv_bfloat16, DD, false, true>(q, k, v, out, prm, stream) \
+                : launch_attn_t<__half, DD, false, true>(q, k, v, out, prm, stream);      \
+    return bf ? launch_attn_t<__nv_bfloat16, DD, false, false>(q, k, v, out, prm, stream)  \
+              : launch_attn_t<__half, DD, false, false>(q, k, v, out, prm, stream);        \
   }
   MI_ATTN_CASE(64)
   MI_ATTN_CASE(96)

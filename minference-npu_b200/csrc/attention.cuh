@@ -59,7 +59,7 @@ struct AttnParams {
   int t_lo, t_n;       // this launch computes tiles [t_lo, t_lo + t_n) (the whole range by default)
   int mode;            // 0: stream/dense arithmetic entries, 1: plan entries
   long long n_init;    // sink length (mode 0; 0 in mode 1)
-  long long n_local;   // window length (mode 0; Sk+1 in mode 1)
+  long long n_local;   // window length (mode 0; 2^40, i.e. unbounded, in mode 1)
   float scale_log2;    // softmax_scale * log2(e)
   void* out;
   long long os_b, os_h, os_s;  // output element strides
@@ -68,6 +68,15 @@ struct AttnParams {
   long long plan_cap;          // mode 1
   long long plan_head_stride;  // mode 1: entries per (b,h)
   int split;                   // 1: split tiles (each half of the tile has its own key block)
+  // mode 1, gathered key groups (vertical_and_slash): a plan entry with
+  // kb = kb1 = -1 - g is group g of its tile, up to 64 scattered keys loaded
+  // row by row (TMA gather4 over a 2-D row view of K and V) whose positions
+  // are gcols[((bh*T+t)*gmax+g)*64 ...] (-1 = empty slot); its masks are the
+  // entry's m0 / m1 as for any entry.
+  int gather;
+  int gmax;
+  const int32_t* gcols;
+  long long grow_b, grow_h;    // row of key 0 of (b, h) in the 2-D row view: b*grow_b + h*grow_h
 };
 
 constexpr int kBM = 128;       // query rows per CTA

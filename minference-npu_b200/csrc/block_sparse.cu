@@ -428,7 +428,7 @@ extern "C" int mi_block_sparse_fwd_rows(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v
   prm.T = (int)T;
   prm.mode = 1;
   prm.n_init = 0;
-  prm.n_local = S + 1;
+  prm.n_local = 1ll << 40;  // unbounded window (see AttnParams)
   prm.scale_log2 = softmax_scale * 1.4426950408889634f;
   prm.plan = plan;
   prm.plan_count = count;

@@ -125,6 +125,19 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Four rows of a 2-D tensor map (box: 32 elements x 1 row) into 4 consecutive
+// 64-byte rows of shared memory (swizzled by address like a 4-row tile).
+__device__ __forceinline__ void tma_gather4_2d(void* smem_dst, const CUtensorMap* map,
+                                               uint64_t* bar, int c0, int r0, int r1, int r2,
+                                               int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cta.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(r0), "r"(r1),
+      "r"(r2), "r"(r3)
+      : "memory");
+}
+
 // Make generic-proxy shared-memory writes visible to the async proxy
 // (tensor core operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -65,6 +65,26 @@ inline int make_bnsd_map(CUtensorMap* map, const mi_tensor4& t, int64_t B, int64
   return r == CUDA_SUCCESS ? MI_OK : MI_ERR_ALIGN;
 }
 
+// 2-D map over `rows` rows of D 16-bit elements, `row_stride` elements apart,
+// with a box of box_d x 1 (the shape tile::gather4 loads take); 64-byte
+// swizzle like the 4-D maps.
+inline int make_rows_map(CUtensorMap* map, void* ptr, int64_t rows, int64_t row_stride,
+                         int64_t D, int box_d) {
+  auto enc = get_encode_tiled();
+  if (!enc) return MI_ERR_LAUNCH;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (row_stride * 2) % 16 || rows <= 0 ||
+      rows >= (1ll << 31))
+    return MI_ERR_ALIGN;
+  cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(row_stride * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)box_d, 1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, ptr, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MI_OK : MI_ERR_ALIGN;
+}
+
 // With MI_DEBUG=1 in the environment, a failed kernel launch prints the CUDA
 // error and the kernel's resource attributes to stderr (the C ABI itself only
 // returns MI_ERR_LAUNCH).

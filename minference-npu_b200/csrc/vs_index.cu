@@ -390,15 +390,16 @@ __global__ void __launch_bounds__(1024) vs_tables_kernel(const int32_t* v_idx, i
     clow[bq] = any_slash(ss, (long long)bq * 64 + 1, (long long)bq * 64 + 63, S) ? 1 : 0;
 }
 
-__device__ __forceinline__ uint64_t vs_block_mask(int bq, int kb, int S, int nb, const SlashSet& P,
-                                                  const unsigned long long* vmask,
+// Slash coverage of key block kb for query block bq (the direct mask
+// without the vertical columns).
+__device__ __forceinline__ uint64_t vs_slash_mask(int bq, int kb, int S, int nb, const SlashSet& P,
                                                   const uint32_t* smask, const int* clow) {
-  uint64_t m = vmask[kb];
-  if (kb == 0 && clow[bq]) m = ~0ull;
+  if (kb == 0 && clow[bq]) return ~0ull;
+  uint64_t m = 0;
   const bool ragged_last = (bq == nb - 1) && (S % 64 != 0);
   if (!ragged_last) {
     const int Dl = bq - kb;
-    m |= (uint64_t)smask[2 * Dl] | ((uint64_t)smask[2 * Dl + 1] << 32);
+    m = (uint64_t)smask[2 * Dl] | ((uint64_t)smask[2 * Dl + 1] << 32);
   } else {
     const long long end_m = (long long)nb * 64;
     const long long lo_bound = end_m - S;  // slashes below this are clamped to [S-64, S)
@@ -416,14 +417,30 @@ __device__ __forceinline__ uint64_t vs_block_mask(int bq, int kb, int S, int nb,
   return m;
 }
 
+// Gathered key groups of a tile (see AttnParams::gather).
+struct VsGather {
+  int gmax;              // groups per tile (0: gathering off)
+  int32_t* gcols;        // [BH][T][gmax][64]
+  unsigned long long* gmask;  // [BH][T][gmax][2], scratch for the masks
+};
+
 // K4b: plan.  One warp per 128-row query tile; entries in ascending kb.
+// With gathering on, the vertical columns of a key block that no slash of
+// either query block reaches (and that lies before both) are listed among
+// the tile's gathered keys instead (with a visibility bit per query block),
+// so a block touched only by scattered columns costs no 64-key step; blocks
+// that are entries anyway keep their columns in their masks.  The groups
+// follow the tile's block entries as entries with kb = -1 - g.  A group holds
+// at least one column of each block it replaces and at most 64 columns, so
+// groups never outnumber the blocks they replace and the tile's entries stay
+// within its 2t + 2 plan slots.
 __global__ void __launch_bounds__(128) vs_plan_kernel(int H, int S, int nb, int T,
                                                       const int* Pall,
                                                       const unsigned long long* vmask_all,
                                                       const uint32_t* smask_all,
                                                       const int* clow_all, long long cap,
                                                       long long head_stride, PlanEntry* plan,
-                                                      int* plan_count) {
+                                                      int* plan_count, VsGather g) {
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 4 + w;
   const int h = blockIdx.y, b = blockIdx.z, bh = b * H + h;
@@ -436,13 +453,33 @@ __global__ void __launch_bounds__(128) vs_plan_kernel(int H, int S, int nb, int 
   const int bq0 = 2 * t, bq1 = 2 * t + 1;
   const int hi = min(bq1, nb - 1);
   PlanEntry* out = plan + (long long)bh * head_stride + plan_offset(t, cap);
-  int count = 0;
+  const long long gt = (long long)bh * T + t;
+  int32_t* gcols = g.gmax ? g.gcols + gt * g.gmax * 64 : nullptr;
+  unsigned long long* gmask = g.gmax ? g.gmask + gt * g.gmax * 2 : nullptr;
+  if (g.gmax) {
+    for (int i = lane; i < g.gmax * 64; i += 32) gcols[i] = -1;
+    for (int i = lane; i < g.gmax * 2; i += 32) gmask[i] = 0ull;
+    __syncwarp();
+  }
+  int count = 0, gtotal = 0;
   for (int base = 0; base <= hi; base += 32) {
     const int kb = base + lane;
-    uint64_t m0 = 0, m1 = 0;
+    uint64_t m0 = 0, m1 = 0, u0 = 0, u1 = 0;
     if (kb <= hi) {
-      if (bq0 < nb && kb <= bq0) m0 = vs_block_mask(bq0, kb, S, nb, P, vmask, smask, clow);
-      if (bq1 < nb && kb <= bq1) m1 = vs_block_mask(bq1, kb, S, nb, P, vmask, smask, clow);
+      const uint64_t vm = vmask[kb];
+      const uint64_t v0 = (bq0 < nb && kb <= bq0) ? vm : 0ull;
+      const uint64_t v1 = (bq1 < nb && kb <= bq1) ? vm : 0ull;
+      if (bq0 < nb && kb <= bq0) m0 = vs_slash_mask(bq0, kb, S, nb, P, smask, clow);
+      if (bq1 < nb && kb <= bq1) m1 = vs_slash_mask(bq1, kb, S, nb, P, smask, clow);
+      if (g.gmax && (m0 | m1) == 0ull && kb < bq0) {
+        // no slash reaches this block (which lies before both query blocks):
+        // its columns are gathered instead of costing a 64-key step
+        u0 = v0;
+        u1 = v1;
+      } else {
+        m0 |= v0;
+        m1 |= v1;
+      }
     }
     const bool keep = (m0 | m1) != 0ull;
     const unsigned bal = __ballot_sync(0xffffffffu, keep);
@@ -455,8 +492,47 @@ __global__ void __launch_bounds__(128) vs_plan_kernel(int H, int S, int nb, int 
       out[count + __popc(bal & ((1u << lane) - 1u))] = e;
     }
     count += __popc(bal);
+    if (g.gmax) {
+      // gathered keys in ascending order: this lane's block after the lower lanes'
+      uint64_t un = u0 | u1;
+      const int n = __popcll(un);
+      int off = n;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, off, d);
+        if (lane >= d) off += y;
+      }
+      const int tot = __shfl_sync(0xffffffffu, off, 31);
+      int idx = gtotal + off - n;
+      while (un) {
+        const int c = __ffsll((long long)un) - 1;
+        un &= un - 1;
+        const int gi = idx >> 6, slot = idx & 63;
+        if (gi < g.gmax) {
+          gcols[gi * 64 + slot] = kb * 64 + c;
+          if ((u0 >> c) & 1ull) atomicOr(&gmask[2 * gi], 1ull << slot);
+          if ((u1 >> c) & 1ull) atomicOr(&gmask[2 * gi + 1], 1ull << slot);
+        }
+        ++idx;
+      }
+      gtotal += tot;
+    }
   }
-  if (lane == 0) plan_count[(long long)bh * T + t] = count;
+  if (g.gmax) {
+    __syncwarp();
+    __threadfence_block();
+    const int ng = min((gtotal + 63) / 64, g.gmax);
+    for (int gi = lane; gi < ng; gi += 32) {
+      PlanEntry e;
+      e.kb = -1 - gi;
+      e.kb1 = e.kb;
+      e.m0 = __ldcg(&gmask[2 * gi]);  // L2: the atomics above
+      e.m1 = __ldcg(&gmask[2 * gi + 1]);
+      out[count + gi] = e;
+    }
+    count += ng;
+  }
+  if (lane == 0) plan_count[gt] = count;
 }
 
 
@@ -549,8 +625,16 @@ struct VsWs {
   int* clow;
   PlanEntry* plan;
   int* count;
+  int32_t* gcols;
+  unsigned long long* gmask;
   size_t bytes;
 };
+
+// Gathered key groups per tile: vertical_size up to kVsGatherCols columns are
+// gathered (kVsGatherMax groups of 64); larger vertical sets keep the columns
+// in their blocks' masks.
+constexpr int kVsGatherMax = 16;
+constexpr int kVsGatherCols = kVsGatherMax * 64;
 
 static VsWs vs_ws_layout(void* base, int64_t B, int64_t H, int64_t S) {
   const int64_t nb = (S + 63) / 64, T = (S + 127) / 128;
@@ -565,6 +649,8 @@ static VsWs vs_ws_layout(void* base, int64_t B, int64_t H, int64_t S) {
   w.clow = reinterpret_cast<int*>(take(4ull * B * H * nb));
   w.plan = reinterpret_cast<PlanEntry*>(take(sizeof(PlanEntry) * B * H * plan_offset(T, cap)));
   w.count = reinterpret_cast<int*>(take(4ull * B * H * T));
+  w.gcols = reinterpret_cast<int32_t*>(take(4ull * B * H * T * kVsGatherMax * 64));
+  w.gmask = reinterpret_cast<unsigned long long*>(take(16ull * B * H * T * kVsGatherMax));
   w.bytes = off;
   return w;
 }
@@ -593,9 +679,23 @@ extern "C" int mi_vs_sparse_fwd_rows(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, m
   const int64_t head_stride = plan_offset(T, cap);
   vs_tables_kernel<<<dim3((unsigned)H, (unsigned)B), 1024, 0, st>>>(
       v_idx, (int)nv, s_idx, (int)ns, (int)H, (int)S, (int)nb, w.P, w.vmask, w.smask, w.clow);
+  // Gathered keys need K and V rows addressable as one 2-D row view: every
+  // (b, h) starts a whole number of rows after the base pointer.
+  static const bool gather_env = [] {
+    const char* e = getenv("MI_VS_GATHER");
+    return !(e && e[0] == '0');
+  }();
+  auto row_view = [](const mi_tensor4& t) {
+    return t.stride_s > 0 && t.stride_h % t.stride_s == 0 && t.stride_b % t.stride_s == 0 &&
+           t.stride_h >= 0 && t.stride_b >= 0;
+  };
+  const bool gather = gather_env && nv <= kVsGatherCols && row_view(k) && row_view(v) &&
+                      k.stride_s == v.stride_s && k.stride_h == v.stride_h &&
+                      k.stride_b == v.stride_b;
+  VsGather vg{gather ? kVsGatherMax : 0, w.gcols, w.gmask};
   dim3 g((unsigned)((T + 3) / 4), (unsigned)H, (unsigned)B);
   vs_plan_kernel<<<g, 128, 0, st>>>((int)H, (int)S, (int)nb, (int)T, w.P, w.vmask, w.smask,
-                                    w.clow, cap, head_stride, w.plan, w.count);
+                                    w.clow, cap, head_stride, w.plan, w.count, vg);
   if (cudaGetLastError() != cudaSuccess) return MI_ERR_LAUNCH;
   AttnParams prm{};
   prm.B = (int)B;
@@ -606,12 +706,19 @@ extern "C" int mi_vs_sparse_fwd_rows(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, m
   prm.T = (int)T;
   prm.mode = 1;
   prm.n_init = 0;
-  prm.n_local = S + 1;
+  prm.n_local = 1ll << 40;  // unbounded window (see AttnParams)
   prm.scale_log2 = softmax_scale * 1.4426950408889634f;
   prm.plan = w.plan;
   prm.plan_count = w.count;
   prm.plan_cap = cap;
   prm.plan_head_stride = head_stride;
+  if (gather) {
+    prm.gather = 1;
+    prm.gmax = kVsGatherMax;
+    prm.gcols = w.gcols;
+    prm.grow_b = k.stride_b / k.stride_s;
+    prm.grow_h = k.stride_h / k.stride_s;
+  }
   prm.t_lo = (int)(row_begin / 128);
   prm.t_n = (int)((row_end + 127) / 128) - prm.t_lo;
   return launch_attention(q, k, v, out, D, dtype, prm, st);

@@ -138,3 +138,26 @@ def test_dense_128k_sampled(cuda):
                    1 / math.sqrt(96))
     err = (out[0, 0][rows].float() - ref).abs().max().item()
     assert err < TOL, err
+
+
+@pytest.mark.parametrize("S,nv,ns", [(8192, 1000, 1024), (8192, 64, 300), (3000, 1024, 100),
+                                     (8192, 1500, 512)])
+def test_vs_local_slashes_scattered_verticals(cuda, S, nv, ns):
+    """Structured VS sets as real configs have them: local slashes (the ns
+    nearest diagonals) plus scattered vertical columns that mostly fall
+    outside the slash band (they are gathered row by row; nv > 1024 keeps
+    them in block masks).  Whole heads against the fp32 masked attention."""
+    ops, O = _ops(), _oracle()
+    H = 2
+    q, k, v = gen_qkv(1, H, S, 96, torch.bfloat16, S + nv, sinks=16, device=cuda)
+    g = torch.Generator().manual_seed(nv)
+    vi = torch.stack([torch.cat([torch.arange(30), 30 + torch.randperm(S - 30, generator=g)[:nv - 30]])
+                      .sort().values for _ in range(H)])[None].int()
+    si = torch.stack([torch.arange(ns - 1, -1, -1) for _ in range(H)])[None].int()
+    out = ops.vertical_slash_sparse_attention(q, k, v, vi, si)
+    for h in range(H):
+        mask = torch.as_tensor(O.vs_mask(vi[0, h].numpy(), si[0, h].numpy(), S), device=cuda)
+        logits = (q[0, h].float() @ k[0, h].float().T) * SCALE
+        ref = torch.softmax(logits.masked_fill(~mask, float("-inf")), -1) @ v[0, h].float()
+        err = (out[0, h].float() - ref).abs().max().item()
+        assert err < TOL, f"head {h}: {err}"
