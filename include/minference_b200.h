@@ -54,10 +54,22 @@ extern "C" {
 #define MI_BF16 1
 
 /* A BNSD tensor view: device pointer plus element strides of B, H, S, D.
- * The D stride must be 1. */
+ * The D stride must be 1.
+ *
+ * Head tables: with head_index == NULL, head h of a call is head h of the
+ * view.  Otherwise head_index is a device array of int32 with one entry per
+ * head of the call, and head h of the call is head head_index[h] of the view
+ * (0 <= head_index[h] < head_extent, the number of heads the view holds).
+ * One launch then serves a non-contiguous set of heads -- the heads of one
+ * pattern in a layer -- reading and writing them in place, where the
+ * reference gathers them with index_select and scatters with index_copy_
+ * (minference/modules/minference_forward.py:423-487).  All tensors of a call
+ * (q, k, v and out) must use the same table. */
 typedef struct mi_tensor4 {
   void* ptr;
   int64_t stride_b, stride_h, stride_s, stride_d;
+  const int32_t* head_index;
+  int64_t head_extent;
 } mi_tensor4;
 
 /* Library version string. */

@@ -83,9 +83,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int t = p.t_lo + p.t_n - 1 - blockIdx.x;  // heavy (late) tiles first
-  const int h = blockIdx.y;
+  const int h = blockIdx.y;  // head of the call (plan and workspace index)
   const int b = blockIdx.z;
   const int bh = b * p.H + h;
+  const int hv = p.head_index ? p.head_index[h] : h;  // head of the q/k/v/out views
 #ifdef MI_TRACE
 #ifndef MI_TRACE_HEAD
 #define MI_TRACE_HEAD 0  // head whose heaviest tile is traced
@@ -181,13 +182,13 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       mbar_arrive_expect_tx(q_full, L::kQBytes);
       for (int c = 0; c < NC; ++c)
-        tma_load_4d(smem + L::kQOff + c * (kBM * 64), &tm_q, q_full, c * 32, t * kBM, h, b);
+        tma_load_4d(smem + L::kQOff + c * (kBM * 64), &tm_q, q_full, c * 32, t * kBM, hv, b);
       // A stage holds one key block per entry, or two in a split tile
       // (the block of query rows [0,64), then the block of rows [64,128)).
       // A gathered group (kb < 0; GATHER kernels only) loads its up to 64 key
       // rows four at a time through the 2-D row view; empty slots load key 0
       // of the head, which the group's masks leave invisible.
-      const long long row0 = (long long)b * p.grow_b + (long long)h * p.grow_h;
+      const long long row0 = (long long)b * p.grow_b + (long long)hv * p.grow_h;
       auto gather_rows = [&](uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int g) {
         const int4* cols = reinterpret_cast<const int4*>(gcols + g * 64);
         for (int rg = 0; rg < kBN / 4; ++rg) {
@@ -213,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int hb = 0; hb < L::NB; ++hb)
           for (int c = 0; c < NC; ++c)
             tma_load_4d(dst + hb * L::kKVBytes + c * (kBN * 64), &tm_k, &k_full[st], c * 32,
-                        kb[hb] * kBN, h, b);
+                        kb[hb] * kBN, hv, b);
         return true;
       };
       auto load_v = [&](int j) -> bool {
@@ -231,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int hb = 0; hb < L::NB; ++hb)
           for (int c = 0; c < NC; ++c)
             tma_load_4d(dst + hb * L::kVBytes + c * (kBN * 64), &tm_v, &v_full[st], c * 32,
-                        kb[hb] * kBN, h, b);
+                        kb[hb] * kBN, hv, b);
         return true;
       };
       bool ok = true;
@@ -546,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     named_barrier(1, kBM);
     if (row == 0 && !*abort_flag) {
       for (int c = 0; c < NC; ++c)
-        tma_store_4d(&tm_o, smem + L::kQOff + c * (kBM * 64), c * 32, t * kBM, h, b);
+        tma_store_4d(&tm_o, smem + L::kQOff + c * (kBM * 64), c * 32, t * kBM, hv, b);
       bulk_commit();
       bulk_wait_read0();
     }
@@ -580,8 +581,8 @@ static int launch_attn_t(const mi_tensor4& q, const mi_tensor4& k, const mi_tens
   memset(&tkr, 0, sizeof(tkr));
   memset(&tvr, 0, sizeof(tvr));
   if (GATHER) {
-    const long long rows = (long long)(prm.B - 1) * prm.grow_b + (long long)(prm.H - 1) * prm.grow_h +
-                           prm.Sk;
+    const long long nh = k.head_index ? k.head_extent : prm.H;
+    const long long rows = (long long)(prm.B - 1) * prm.grow_b + (nh - 1) * prm.grow_h + prm.Sk;
     if ((rc = make_rows_map(&tkr, k.ptr, rows, k.stride_s, D, 32)) != MI_OK) return rc;
     if ((rc = make_rows_map(&tvr, v.ptr, rows, v.stride_s, D, 32)) != MI_OK) return rc;
   }
@@ -604,6 +605,11 @@ static int launch_attn_t(const mi_tensor4& q, const mi_tensor4& k, const mi_tens
 int launch_attention(const mi_tensor4& q, const mi_tensor4& k, const mi_tensor4& v,
                      const mi_tensor4& out, int64_t D, int dtype, AttnParams prm,
                      cudaStream_t stream) {
+  // one head table for q, k, v and out (see mi_tensor4)
+  if (k.head_index != q.head_index || v.head_index != q.head_index ||
+      out.head_index != q.head_index)
+    return MI_ERR_SHAPE;
+  prm.head_index = q.head_index;
   prm.out = out.ptr;
   prm.os_b = out.stride_b;
   prm.os_h = out.stride_h;

@@ -68,6 +68,7 @@ struct AttnParams {
   long long plan_cap;          // mode 1
   long long plan_head_stride;  // mode 1: entries per (b,h)
   int split;                   // 1: split tiles (each half of the tile has its own key block)
+  const int32_t* head_index;   // head table of the views, or null (see mi_tensor4)
   // mode 1, gathered key groups (vertical_and_slash): a plan entry with
   // kb = kb1 = -1 - g is group g of its tile, up to 64 scattered keys loaded
   // row by row (TMA gather4 over a 2-D row view of K and V) whose positions
@@ -88,10 +89,16 @@ constexpr int kThreads = 192;
 // Ring depths.  A split tile stages two key blocks per entry (one per query
 // half), so its rings are shallower where two CTAs share an SM (D <= 96; at
 // D = 128 O needs more than half of TMEM and one CTA runs per SM).
+#ifndef MI_SPLIT_KS
+#define MI_SPLIT_KS 2
+#endif
+#ifndef MI_SPLIT_VS96
+#define MI_SPLIT_VS96 1
+#endif
 template <int D, bool SPLIT>
 struct RingDepth {
-  static constexpr int K = SPLIT ? 2 : kKStages;
-  static constexpr int V = SPLIT ? (D == 96 ? 1 : 2) : kVStages;
+  static constexpr int K = SPLIT ? MI_SPLIT_KS : kKStages;
+  static constexpr int V = SPLIT ? (D == 96 ? MI_SPLIT_VS96 : 2) : kVStages;
 };
 
 template <int D, bool SPLIT = false>
@@ -133,7 +140,9 @@ struct AttnSmem {
   // +1 KiB to align the base; never less than ~80 KiB so at most two CTAs
   // share an SM (two CTAs use all 512 TMEM columns).
   static constexpr int kAlloc = (kBytes + 1024) > 80 * 1024 ? (kBytes + 1024) : 80 * 1024;
+#ifndef MI_ONE_CTA_SPLIT
   static_assert(kTmemCols == 512 || kAlloc <= 113 * 1024, "two CTAs per SM");
+#endif
 };
 
 // Entry j of the current tile (identical result in every warp that asks).

@@ -34,7 +34,7 @@ __global__ void __launch_bounds__(256) pool_kernel(mi_tensor4 q, mi_tensor4 k, i
   if (blk >= nb) return;
   const mi_tensor4& t = is_k ? k : q;
   const uint16_t* base = reinterpret_cast<const uint16_t*>(t.ptr) + (long long)b * t.stride_b +
-                         (long long)h * t.stride_h + d;
+                         (long long)view_head(t, h) * t.stride_h + d;
   const int r0 = blk * 64;
   const int rn = min(64, S - r0);
   float vals[64];
@@ -72,7 +72,8 @@ __global__ void __launch_bounds__(128) pool_kernel_v(mi_tensor4 q, mi_tensor4 k,
   if (u >= 8 || blk >= nb) return;
   const mi_tensor4& t = is_k ? k : q;
   const uint16_t* base = reinterpret_cast<const uint16_t*>(t.ptr) + (long long)b * t.stride_b +
-                         (long long)h * t.stride_h + (long long)blk * 64 * t.stride_s + c * 8;
+                         (long long)view_head(t, h) * t.stride_h + (long long)blk * 64 * t.stride_s +
+                         c * 8;
   const int rn = min(64, S - blk * 64);
   float acc[8];
 #pragma unroll

@@ -138,6 +138,11 @@ __device__ __forceinline__ void tma_gather4_2d(void* smem_dst, const CUtensorMap
       : "memory");
 }
 
+// Head of the view that head h of a call addresses (see mi_tensor4).
+__device__ __forceinline__ int view_head(const mi_tensor4& t, int h) {
+  return t.head_index ? t.head_index[h] : h;
+}
+
 // Make generic-proxy shared-memory writes visible to the async proxy
 // (tensor core operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -46,6 +46,10 @@ inline int make_bnsd_map(CUtensorMap* map, const mi_tensor4& t, int64_t B, int64
   if (t.stride_d != 1) return MI_ERR_ALIGN;
   if (reinterpret_cast<uintptr_t>(t.ptr) & 15) return MI_ERR_ALIGN;
   const int64_t es = 2;
+  if (t.head_index) {  // the map spans every head of the view; the kernel picks them
+    if (t.head_extent < 1) return MI_ERR_SHAPE;
+    H = t.head_extent;
+  }
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
   int64_t st[3] = {t.stride_s * es, t.stride_h * es, t.stride_b * es};
   cuuint64_t strides[3];

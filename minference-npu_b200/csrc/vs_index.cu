@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(128) vs_logits_kernel(mi_tensor4 q, mi_tensor4
   const int h = blockIdx.y, b = blockIdx.z, bh = b * H + h;
   const int key0 = blockIdx.x * kLgKeys;
   const uint16_t* qb = reinterpret_cast<const uint16_t*>(q.ptr) + (long long)b * q.stride_b +
-                       (long long)h * q.stride_h;
+                       (long long)view_head(q, h) * q.stride_h;
   // Q tile: 16-byte loads (8 dims of one row), all issued before the
   // transposed fp32 stores; consecutive threads take consecutive rows, so
   // the stores are conflict-free.
@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(128) vs_logits_kernel(mi_tensor4 q, mi_tensor4
   {
     const int c = key0 + threadIdx.x;
     const uint16_t* kr = reinterpret_cast<const uint16_t*>(k.ptr) + (long long)b * k.stride_b +
-                         (long long)h * k.stride_h + (long long)c * k.stride_s;
+                         (long long)view_head(k, h) * k.stride_h + (long long)c * k.stride_s;
 #pragma unroll
     for (int d = 0; d < D; d += 8) {
       uint4 raw = make_uint4(0u, 0u, 0u, 0u);

@@ -42,6 +42,8 @@ class mi_tensor4(ctypes.Structure):
         ("stride_h", ctypes.c_int64),
         ("stride_s", ctypes.c_int64),
         ("stride_d", ctypes.c_int64),
+        ("head_index", ctypes.c_void_p),
+        ("head_extent", ctypes.c_int64),
     ]
 
 
@@ -108,9 +110,13 @@ def check(rc: int, what: str) -> None:
         raise MInferenceNativeError(f"{what} failed: status {rc} ({_STATUS.get(rc, 'unknown')})")
 
 
-def t4(x: torch.Tensor) -> mi_tensor4:
+def t4(x: torch.Tensor, heads: torch.Tensor | None = None) -> mi_tensor4:
+    """View descriptor of a BNSD tensor; `heads` (device int32) selects the
+    heads a call addresses (see mi_tensor4 in the header)."""
     s = x.stride()
-    return mi_tensor4(x.data_ptr(), s[0], s[1], s[2], s[3])
+    if heads is None:
+        return mi_tensor4(x.data_ptr(), s[0], s[1], s[2], s[3], None, 0)
+    return mi_tensor4(x.data_ptr(), s[0], s[1], s[2], s[3], heads.data_ptr(), x.shape[1])
 
 
 def dtype_code(x: torch.Tensor) -> int:

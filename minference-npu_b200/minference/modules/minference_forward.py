@@ -15,9 +15,10 @@ minference/modules/minference_forward.py:175-502):
 * ``o_proj`` on the re-assembled heads (:492-494).
 
 Differences in how the work is laid out (results are the same): a group
-whose heads form a contiguous range is passed as a strided view and written
-in place into the layer output (no ``index_select`` / ``index_copy_``);
-other groups gather their heads.  The layer output is allocated in the
+whose heads form a contiguous range is passed as a strided view, any other
+group as the whole layer plus a device head table, so each group is one
+launch per kernel that reads its heads and writes the layer output in place
+(no ``index_select`` / ``index_copy_``).  The layer output is allocated in the
 ``[B, S, H, D]`` layout ``o_proj`` consumes, and the ops write into its
 ``[B, H, S, D]`` view.
 """
@@ -192,16 +193,19 @@ def init_minference_parameters(self) -> None:
 # ----------------------------------------------------------------------------
 
 
-def _run_pattern(key, q, k, v, out=None):
+def _run_pattern(key, q, k, v, out=None, heads=None):
+    """One launch of pattern `key`; `heads` (optional) picks the heads of
+    q/k/v/out it runs on, written in place into `out`."""
     ty = key[0]
+    kw = {} if heads is None else {"heads": heads}
     if ty == "vertical_and_slash":
-        return OPS.vertical_and_slash(q, k, v, key[1], key[2], out=out)
+        return OPS.vertical_and_slash(q, k, v, key[1], key[2], out=out, **kw)
     if ty == "stream_llm":
-        return OPS.streaming_forward(q, k, v, key[1], key[2], out=out)
+        return OPS.streaming_forward(q, k, v, key[1], key[2], out=out, **kw)
     if ty == "block_sparse":
-        return OPS.block_sparse_attention(q, k, v, key[1], out=out)
+        return OPS.block_sparse_attention(q, k, v, key[1], out=out, **kw)
     if ty == "dense":
-        return OPS.dense_attention(q, k, v, causal=True, out=out)
+        return OPS.dense_attention(q, k, v, causal=True, out=out, **kw)
     raise NotImplementedError(f"Unsupported pattern {ty!r}")
 
 
@@ -242,11 +246,24 @@ def attention_heads(self, q, k, v):
             sl = slice(heads[0], heads[-1] + 1)
             _run_pattern(key, q[:, sl], k[:, sl], v[:, sl], out=out[:, sl])
         else:
-            idx = torch.tensor(heads, device=q.device, dtype=torch.long)
-            res = _run_pattern(key, q.index_select(1, idx), k.index_select(1, idx),
-                               v.index_select(1, idx))
-            out.index_copy_(1, idx, res)
+            # one launch over the group through a head table: no gather of
+            # q/k/v and no scatter of the output
+            _run_pattern(key, q, k, v, out=out, heads=_head_table(heads, q.device))
     return out_bshd
+
+
+_HEAD_TABLES: dict = {}
+
+
+def _head_table(heads, device):
+    """Device int32 head table, cached per (heads, device): a layer's groups
+    are the same at every forward."""
+    key = (tuple(heads), str(device))
+    t = _HEAD_TABLES.get(key)
+    if t is None:
+        t = torch.tensor(heads, dtype=torch.int32, device=device)
+        _HEAD_TABLES[key] = t
+    return t
 
 
 def minference_forward():

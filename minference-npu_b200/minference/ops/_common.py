@@ -74,10 +74,14 @@ def check_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
     _native.dtype_code(q)
 
 
-def output(out: torch.Tensor | None, shape: tuple, like: torch.Tensor) -> torch.Tensor:
-    """The output tensor: a new one, or a caller-provided [B,H,S,D] view (any
-    strides with unit D stride and 16-byte aligned rows) written in place."""
+def output(out: torch.Tensor | None, shape: tuple, like: torch.Tensor,
+           zero: bool = False) -> torch.Tensor:
+    """The output tensor: a new one (zero-filled if `zero`, for calls that
+    write only some heads), or a caller-provided [B,H,S,D] view (any strides
+    with unit D stride and 16-byte aligned rows) written in place."""
     if out is None:
+        if zero:
+            return torch.zeros(shape, dtype=like.dtype, device=like.device)
         return torch.empty(shape, dtype=like.dtype, device=like.device)
     if tuple(out.shape) != tuple(shape) or out.dtype != like.dtype or out.device != like.device:
         raise ValueError(
@@ -100,3 +104,20 @@ def row_window(rows, S: int) -> tuple[int, int]:
         raise ValueError(f"rows={rows!r}: need 0 <= begin <= end <= S={S}, begin a multiple of "
                          "128 and end a multiple of 128 or S")
     return r0, r1
+
+
+def head_table(heads, q: torch.Tensor):
+    """(device int32 table or None, number of heads the call addresses).
+
+    ``heads`` lists heads of q's head dimension (a sequence or an integer
+    tensor); the op then runs on those heads only, in place, with one launch
+    (the kernels index the views through the table)."""
+    H = q.shape[1]
+    if heads is None:
+        return None, H
+    t = torch.as_tensor(heads, dtype=torch.int32).flatten()
+    if t.numel() == 0:
+        return t.to(q.device), 0
+    if bool((t < 0).any()) or bool((t >= H).any()):
+        raise ValueError(f"heads must lie in [0, {H}); got {t.tolist()}")
+    return t.to(q.device), int(t.numel())

@@ -15,7 +15,8 @@ import math
 import torch
 
 from .. import _native
-from ._common import check_qkv, default_softmax_scale, kernel_dim, prepare, row_window
+from ._common import (check_qkv, default_softmax_scale, head_table, kernel_dim, prepare,
+                      row_window)
 from ._common import output as _common_out
 
 __all__ = [
@@ -29,10 +30,12 @@ LAST_Q = 64
 
 
 def vertical_and_slash_estimate(q: torch.Tensor, k: torch.Tensor, vertical_size: int,
-                                slash_size: int) -> tuple[torch.Tensor, torch.Tensor]:
-    """(v_idx int32 [B,H,nv] ascending, s_idx int32 [B,H,ns] descending) from the last 64 queries."""
+                                slash_size: int, heads=None) -> tuple[torch.Tensor, torch.Tensor]:
+    """(v_idx int32 [B,H,nv] ascending, s_idx int32 [B,H,ns] descending) from the
+    last 64 queries; ``heads`` selects heads of q/k (one launch per kernel)."""
     _native.require_cuda(q, k)
-    B, H, S, D = q.shape
+    B, _, S, D = q.shape
+    tbl, H = head_table(heads, q)
     nv = min(S, max(int(vertical_size), 30))
     ns = min(S, max(int(slash_size), 50))
     dk = kernel_dim(D)
@@ -40,10 +43,12 @@ def vertical_and_slash_estimate(q: torch.Tensor, k: torch.Tensor, vertical_size:
     qp, kp = prepare(q, dk), prepare(k, dk)
     v_idx = torch.empty((B, H, nv), dtype=torch.int32, device=q.device)
     s_idx = torch.empty((B, H, ns), dtype=torch.int32, device=q.device)
+    if H == 0:
+        return v_idx, s_idx
     ws = _native.workspace(_native.lib().mi_vs_estimate_workspace_size(B, H, S), q.device)
     with torch.cuda.device(q.device):
         rc = _native.lib().mi_vs_estimate(
-            _native.t4(qp), _native.t4(kp), B, H, S, dk, _native.dtype_code(q), nv, ns,
+            _native.t4(qp, tbl), _native.t4(kp, tbl), B, H, S, dk, _native.dtype_code(q), nv, ns,
             logit_scale, v_idx.data_ptr(), s_idx.data_ptr(), ws.data_ptr(), ws.numel(),
             _native.stream_ptr(q.device),
         )
@@ -56,15 +61,19 @@ def vertical_slash_sparse_attention(query: torch.Tensor, key: torch.Tensor, valu
                                     block_size_M: int = 64, block_size_N: int = 64,
                                     softmax_scale: float | None = None, *,
                                     out: torch.Tensor | None = None,
-                                    rows: tuple[int, int] | None = None) -> torch.Tensor:
+                                    rows: tuple[int, int] | None = None,
+                                    heads=None) -> torch.Tensor:
     """Vertical-slash causal attention; same signature as the reference op.
 
     ``rows=(begin, end)`` computes only those query rows (whole 128-row tiles,
-    the end may be S); the other rows of the output are left as they are."""
+    the end may be S); the other rows of the output are left as they are.
+    ``heads`` runs only those heads in one launch (v_idx / s_idx then have
+    ``len(heads)`` heads, in that order) and writes them in place."""
     check_qkv(query, key, value)
     if block_size_M != 64 or block_size_N != 64:
         raise NotImplementedError("block_size_M/N must be 64")
-    B, H, S, D = query.shape
+    B, Hf, S, D = query.shape
+    tbl, H = head_table(heads, query)
     assert key.shape[2] == S, (
         f"vertical_slash_sparse_attention supports full prefill only (S_q == S_k); "
         f"got S_q={S}, S_k={key.shape[2]}"
@@ -75,11 +84,14 @@ def vertical_slash_sparse_attention(query: torch.Tensor, key: torch.Tensor, valu
     vi = v_idx.to(device=query.device, dtype=torch.int32).reshape(B, H, -1).contiguous()
     si = s_idx.to(device=query.device, dtype=torch.int32).reshape(B, H, -1).contiguous()
     qp, kp, vp = prepare(query, dk), prepare(key, dk), prepare(value, dk)
-    out = _common_out(out, (B, H, S, dk), query)
+    out = _common_out(out, (B, Hf, S, dk), query, zero=tbl is not None)
+    if H == 0:
+        return out[..., :D] if dk != D else out
     ws = _native.workspace(_native.lib().mi_vs_sparse_fwd_workspace_size(B, H, S), query.device)
     with torch.cuda.device(query.device):
         rc = _native.lib().mi_vs_sparse_fwd_rows(
-            _native.t4(qp), _native.t4(kp), _native.t4(vp), _native.t4(out), B, H, S, dk,
+            _native.t4(qp, tbl), _native.t4(kp, tbl), _native.t4(vp, tbl), _native.t4(out, tbl),
+            B, H, S, dk,
             _native.dtype_code(query), vi.data_ptr(), vi.shape[-1], si.data_ptr(), si.shape[-1],
             scale, r0, r1, ws.data_ptr(), ws.numel(), _native.stream_ptr(query.device),
         )
@@ -89,10 +101,11 @@ def vertical_slash_sparse_attention(query: torch.Tensor, key: torch.Tensor, valu
 
 def vertical_and_slash(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, vertical_size: int,
                        slash_size: int, *, out: torch.Tensor | None = None,
-                       rows: tuple[int, int] | None = None) -> torch.Tensor:
+                       rows: tuple[int, int] | None = None, heads=None) -> torch.Tensor:
     """Estimate indices from the last 64 queries, then run the sparse attention."""
-    v_idx, s_idx = vertical_and_slash_estimate(q, k, vertical_size, slash_size)
-    return vertical_slash_sparse_attention(q, k, v, v_idx, s_idx, out=out, rows=rows)
+    v_idx, s_idx = vertical_and_slash_estimate(q, k, vertical_size, slash_size, heads=heads)
+    return vertical_slash_sparse_attention(q, k, v, v_idx, s_idx, out=out, rows=rows,
+                                           heads=heads)
 
 
 def convert_vertical_slash_indexes(seqlens: torch.Tensor, vertical_indexes: torch.Tensor,

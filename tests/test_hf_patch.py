@@ -57,29 +57,37 @@ class StubOps:
 
         return default_softmax_scale(d)
 
-    def _write(self, res, out):
+    def _write(self, res, out, q, heads):
         res = res.to(torch.float32)
+        if heads is not None:  # one call over a head table: write those heads in place
+            idx = torch.as_tensor(heads, dtype=torch.long)
+            full = out if out is not None else torch.zeros(q.shape, dtype=torch.float32)
+            full.index_copy_(1, idx, res[:, idx].to(full.dtype))
+            return full
         if out is not None:
             out.copy_(res.to(out.dtype))
             return out
         return res
 
-    def dense_attention(self, q, k, v, *, scale=None, causal=True, out=None):
-        self.calls.append(("dense", q.shape[1]))
+    def _n(self, q, heads):
+        return q.shape[1] if heads is None else len(heads)
+
+    def dense_attention(self, q, k, v, *, scale=None, causal=True, out=None, heads=None):
+        self.calls.append(("dense", self._n(q, heads)))
         sc = 1.0 / math.sqrt(q.shape[-1]) if scale is None else scale
-        return self._write(_causal_fp32(q, k, v, sc), out)
+        return self._write(_causal_fp32(q, k, v, sc), out, q, heads)
 
-    def streaming_forward(self, q, k, v, n_init, n_local, out=None):
-        self.calls.append(("stream_llm", q.shape[1], n_init, n_local))
-        return self._write(_causal_fp32(q, k, v, self._scale(q.shape[-1])), out)
+    def streaming_forward(self, q, k, v, n_init, n_local, out=None, heads=None):
+        self.calls.append(("stream_llm", self._n(q, heads), n_init, n_local))
+        return self._write(_causal_fp32(q, k, v, self._scale(q.shape[-1])), out, q, heads)
 
-    def block_sparse_attention(self, q, k, v, topk, out=None):
-        self.calls.append(("block_sparse", q.shape[1], topk))
-        return self._write(_causal_fp32(q, k, v, self._scale(q.shape[-1])), out)
+    def block_sparse_attention(self, q, k, v, topk, out=None, heads=None):
+        self.calls.append(("block_sparse", self._n(q, heads), topk))
+        return self._write(_causal_fp32(q, k, v, self._scale(q.shape[-1])), out, q, heads)
 
-    def vertical_and_slash(self, q, k, v, vs, ss, out=None):
-        self.calls.append(("vertical_and_slash", q.shape[1], vs, ss))
-        return self._write(_causal_fp32(q, k, v, self._scale(q.shape[-1])), out)
+    def vertical_and_slash(self, q, k, v, vs, ss, out=None, heads=None):
+        self.calls.append(("vertical_and_slash", self._n(q, heads), vs, ss))
+        return self._write(_causal_fp32(q, k, v, self._scale(q.shape[-1])), out, q, heads)
 
 
 @pytest.fixture
@@ -130,7 +138,7 @@ def test_grouping_follows_pattern_config(stub, tmp_path):
     # padded-D scale, so the logits differ from HF's but stay finite
     assert torch.isfinite(out).all() and out.shape == ref.shape
     calls = stub.calls
-    assert ("stream_llm", 2, 4, 16) in calls          # heads 0 and 2 batched (gathered)
+    assert ("stream_llm", 2, 4, 16) in calls          # heads 0 and 2: one call, head table
     assert ("block_sparse", 1, 3) in calls
     assert ("dense", 1) in calls
     assert ("vertical_and_slash", 1, 40, 60) in calls
