@@ -452,6 +452,7 @@ class TileLayer:
         self.q, self.k, self.v = make_inputs(self.heads, S, device)
         self.out = torch.zeros(1, n_heads, S, D, dtype=torch.bfloat16, device=device)
         self.comm = torch.cuda.Stream(device=device)
+        self.streams = [torch.cuda.Stream(device=device) for _ in range(4)]
 
     def _batches(self, pieces):
         """Consecutive whole-head pieces of one pattern run as one launch
@@ -469,7 +470,14 @@ class TileLayer:
         return batches
 
     def _run_pieces(self, pieces, est, q, k, v, ev):
+        """Index estimation of every batch on the current stream, then the
+        attention launches side by side on separate streams: a rank's launches
+        are few and small (parts of a head), and each one's critical path is
+        its heaviest tile, so running them concurrently lets their tails
+        overlap.  ev gets one (start, end) pair spanning the attention."""
         ops = self.ops
+        main = torch.cuda.current_stream(self.device)
+        jobs = []
         for p, slots, _full, rows in self._batches(pieces):
             a, b = self.local[slots[0]], self.local[slots[-1]] + 1
             qs, ks, vs = q[:, a:b], k[:, a:b], v[:, a:b]
@@ -480,23 +488,36 @@ class TileLayer:
                 if key not in est:
                     est[key] = ops.vertical_and_slash_estimate(qs, ks, VS_V, VS_S)
                 vi, si = est[key]
-                e0 = Layer._ev(ev)
-                ops.vertical_slash_sparse_attention(qs, ks, vs, vi, si, out=os_, rows=rw)
+                jobs.append(lambda qs=qs, ks=ks, vs=vs, vi=vi, si=si, os_=os_, rw=rw:
+                            ops.vertical_slash_sparse_attention(qs, ks, vs, vi, si, out=os_,
+                                                                rows=rw))
             elif p == "block_sparse":
                 if key not in est:
                     est[key] = ops.select_block_sparse_topk_indices(qs, ks, BS_TOPK)
-                e0 = Layer._ev(ev)
-                ops.block_sparse_attention_from_indices(qs, ks, vs, est[key], out=os_, rows=rw)
+                jobs.append(lambda qs=qs, ks=ks, vs=vs, idx=est[key], os_=os_, rw=rw:
+                            ops.block_sparse_attention_from_indices(qs, ks, vs, idx, out=os_,
+                                                                    rows=rw))
             elif p == "stream_llm":
-                e0 = Layer._ev(ev)
-                ops.streaming_forward(qs, ks, vs, ST_INIT, ST_LOCAL, out=os_, rows=rw)
+                jobs.append(lambda qs=qs, ks=ks, vs=vs, os_=os_, rw=rw:
+                            ops.streaming_forward(qs, ks, vs, ST_INIT, ST_LOCAL, out=os_,
+                                                  rows=rw))
             else:
-                e0 = Layer._ev(ev)
-                ops.dense_attention(qs, ks, vs, out=os_, rows=rw)
-            if ev is not None:
-                e1 = torch.cuda.Event(enable_timing=True)
-                e1.record()
-                ev.append((e0, e1))
+                jobs.append(lambda qs=qs, ks=ks, vs=vs, os_=os_, rw=rw:
+                            ops.dense_attention(qs, ks, vs, out=os_, rows=rw))
+        e0 = Layer._ev(ev)
+        fork = torch.cuda.Event()
+        fork.record(main)
+        for i, job in enumerate(jobs):
+            st = self.streams[i % len(self.streams)]
+            st.wait_event(fork)
+            with torch.cuda.stream(st):
+                job()
+        for st in self.streams[:len(jobs)]:
+            main.wait_stream(st)
+        if ev is not None:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record(main)
+            ev.append((e0, e1))
 
     def run(self, q=None, k=None, v=None, ev=None):
         from minference.sharding import gather_row_ranges
@@ -506,6 +527,9 @@ class TileLayer:
         v = self.v if v is None else v
         first, second = self.halves[self.rank]
         est = {}
+        if not torch.distributed.is_initialized():  # --sim-rank: this rank's compute only
+            self._run_pieces(first + second, est, q, k, v, ev)
+            return self.out
         self._run_pieces(first, est, q, k, v, ev)
         main = torch.cuda.current_stream(self.device)
         self.comm.wait_stream(main)
@@ -515,6 +539,13 @@ class TileLayer:
         gather_row_ranges(self.out, [h[1] for h in self.halves])
         main.wait_stream(self.comm)
         return self.out
+
+    def own_span(self):
+        """This rank's units as a flat view of the output (one contiguous block)."""
+        from minference.sharding import _flat_span
+
+        sp = _flat_span(self.parts[self.rank], self.S, D)
+        return self.out.view(-1)[sp[0]:sp[1]] if sp else self.out.view(-1)[:0]
 
     def launches_per_step(self) -> int:
         n = 0
@@ -553,7 +584,7 @@ ATTN_DRAM_BYTES_PER_HEAD_64K = {"vertical_and_slash": 49.4e6, "block_sparse": 42
 
 
 def attn_traffic_bytes(layer, S: int):
-    if S != 65536:
+    if S != 65536 or not hasattr(layer, "slices"):
         return None
     tot = 0.0
     for p, sl in layer.slices:
@@ -1058,9 +1089,13 @@ def main():
                          "the whole gather (serial) or chunk by chunk behind it (overlap)")
     ap.add_argument("--head-map", default="balanced", choices=["balanced", "contiguous"],
                     help="head -> rank map for N>1 with --partition heads (minference.sharding)")
-    ap.add_argument("--partition", default="tiles", choices=["tiles", "heads"],
-                    help="N>1: split (head, query-tile) units of equal modelled cost over the "
-                         "ranks (tiles), or whole heads (heads)")
+    ap.add_argument("--sim-world", type=int, default=0,
+                    help="diagnostic: on one GPU, time only rank --sim-rank's compute of a "
+                         "--sim-world-GPU tile partition (no exchange)")
+    ap.add_argument("--sim-rank", type=int, default=0)
+    ap.add_argument("--partition", default="heads", choices=["heads", "tiles"],
+                    help="N>1: whole heads per rank (heads, cost-balanced map), or (head, "
+                         "query-tile) units of equal modelled cost (tiles)")
     ap.add_argument("--baseline-configs", action="store_true",
                     help="BASELINE configs 0-2 as single-layer ops (one JSON line each)")
     args = ap.parse_args()
@@ -1102,14 +1137,17 @@ def main():
     # the attention of the rest.
     tiles = world > 1 and args.o_proj == "none" and args.partition == "tiles"
     split_gather = world > 1 and args.o_proj == "none" and not tiles
-    if tiles:
+    if args.sim_world > 1:  # one GPU computes rank sim_rank's share of a sim_world-GPU step
+        tiles = True
+        layer = TileLayer(args.sim_rank, args.sim_world, S, device, args.pattern, args.heads)
+    elif tiles:
         layer = TileLayer(rank, world, S, device, args.pattern, args.heads)
     else:
         layer = Layer(rank, world, S, device, args.pattern, args.heads, head_map,
                       head_major_out=split_gather)
     n_heads = args.heads
     gathered = None
-    if world > 1 and not split_gather:
+    if world > 1 and not split_gather and not tiles:
         gathered = torch.empty((world,) + tuple(layer.out_bshd.shape), dtype=torch.bfloat16,
                                device=device)
     if split_gather:
@@ -1215,7 +1253,7 @@ def main():
     pin_k = layer.k.cpu().pin_memory()
     pin_v = layer.v.cpu().pin_memory()
     e_steps = max(2, min(args.steps, 5))
-    if world == 1 and args.o_proj == "none":
+    if world == 1 and args.o_proj == "none" and not args.sim_world:
         from minference.host_pipeline import layer_attention_from_host
 
         pin_o = torch.empty(tuple(layer.q.shape), dtype=torch.bfloat16).pin_memory()
@@ -1224,16 +1262,19 @@ def main():
         def e2e_step():
             layer_attention_from_host(pin_q, pin_k, pin_v, pin_o, layer.run_spec, device)
     else:
-        pin_o = torch.empty(out_shape, dtype=torch.bfloat16).pin_memory()
+        # each rank copies out the part of the layer output it computed
+        own = layer.own_span() if tiles else None
+        pin_o = torch.empty(own.shape if tiles else out_shape,
+                            dtype=torch.bfloat16).pin_memory()
         dq, dk_, dv = torch.empty_like(layer.q), torch.empty_like(layer.k), torch.empty_like(layer.v)
-        e2e_mode = "copy in, step, copy out"
+        e2e_mode = "copy in, step, copy out (each rank its own part of the output)"
 
         def e2e_step():
             dq.copy_(pin_q, non_blocking=True)
             dk_.copy_(pin_k, non_blocking=True)
             dv.copy_(pin_v, non_blocking=True)
             o = step(dq, dk_, dv)
-            pin_o.copy_(o, non_blocking=True)
+            pin_o.copy_(layer.own_span() if tiles else o, non_blocking=True)
     e2e_step()  # warm the pipeline's buffers
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
@@ -1246,6 +1287,10 @@ def main():
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e_steps)
     h2d = 3 * layer.q.numel() * 2
     d2h = pin_o.numel() * 2
+    if world > 1:  # whole-job bytes: ranks may copy different amounts
+        tb = torch.tensor([float(h2d), float(d2h)], device=device, dtype=torch.float64)
+        torch.distributed.all_reduce(tb)
+        h2d, d2h = int(tb[0].item()), int(tb[1].item())
 
     # ---- dense comparator (same heads, dense causal with the same kernel) --------
     barrier()
@@ -1336,8 +1381,8 @@ def main():
             "clocks": clk,
             **({"vs_local": layer.vs_local_stats()} if args.pattern == "vs_local" else {}),
             "e2e": {"value": dense_flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
-                    "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d * world,
-                    "d2h_bytes_per_step": d2h * world, "mode": e2e_mode},
+                    "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "mode": e2e_mode},
             "gpu_launches": layer.launches_per_step() * args.steps,
             "device_error": err,
         }

@@ -234,19 +234,26 @@ def gather_o_proj(local_bshd: torch.Tensor, weight_perm: torch.Tensor, bias=None
 # (head, query-tile) partition
 # ---------------------------------------------------------------------------
 TILE_ROWS = 128
-# fixed cost of one 128-row tile (setup, Q load, epilogue) in units of one
-# 64-key block step of the attention kernel
-TILE_OVERHEAD = 4.0
+# Cost model, in units of one 64-key step of a one-tile (M=128) attention
+# entry, fitted to per-pattern timings of 8 heads x 64K on one B200
+# (vertical_and_slash 0.84 ms, block_sparse 0.205 ms, stream_llm 0.048 ms
+# per head): a tile's fixed cost (set-up, Q load, epilogue), the cost of a
+# block_sparse split-tile step (two M=64 MMAs and a 128-row softmax), and
+# the index estimation of a head, charged to its first tile.
+TILE_OVERHEAD = 8.5
+SPLIT_STEP = 1.25
+HEAD_FIXED = {"vertical_and_slash": 9500.0, "block_sparse": 3000.0}
 
 
 def tile_costs(pattern, S: int) -> list[float]:
     """Modelled cost of each 128-row query tile of one head: the 64-key
-    blocks the attention kernel walks for it, plus a fixed per-tile cost.
+    blocks the attention kernel walks for it, plus a fixed per-tile cost
+    (and the head's index estimation on its first tile).
 
     vertical_and_slash and dense walk the causal blocks (2t + 2 for tile t;
     at long contexts the VS set covers nearly all of them); block_sparse
-    walks max over its two query blocks of min(top-k, causal blocks);
-    stream_llm walks its sink and window blocks."""
+    walks max over its two query blocks of min(top-k, causal blocks) split
+    steps; stream_llm walks its sink and window blocks."""
     ty = pattern[0]
     T = -(-S // TILE_ROWS)
     out = []
@@ -255,13 +262,15 @@ def tile_costs(pattern, S: int) -> list[float]:
         if ty in ("vertical_and_slash", "dense"):
             n = causal
         elif ty == "block_sparse":
-            n = min(max(1, int(pattern[1])), causal)
+            n = SPLIT_STEP * min(max(1, int(pattern[1])), causal)
         elif ty == "stream_llm":
             n_init, n_local = int(pattern[1]), int(pattern[2])
             n = min(causal, -(-n_init // 64) + -(-(n_local + TILE_ROWS) // 64) + 1)
         else:
             raise ValueError(f"unknown pattern type {ty!r}")
         out.append(n + TILE_OVERHEAD)
+    if out:
+        out[0] += HEAD_FIXED.get(ty, 0.0)
     return out
 
 
@@ -351,9 +360,10 @@ def gather_row_ranges(out: torch.Tensor, pieces_per_rank: list[list[Piece]], gro
     """In-place all-gather of row ranges: `out` is a contiguous ``[1, H, S, D]``
     tensor in which this rank has computed its pieces; afterwards every rank
     holds every rank's pieces.  Each rank's pieces must form one contiguous
-    unit range (as `tile_partition` and `unit_range_split` produce).  The
-    exchange is one batch of point-to-point sends and receives (NCCL groups
-    them; gloo runs them as plain sends)."""
+    unit range (as `tile_partition` and `unit_range_split` produce).  With
+    NCCL the exchange is one uneven all-gather whose outputs are the ranges
+    themselves (no staging copy); other backends exchange the ranges with
+    point-to-point sends and receives."""
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     if out.dim() != 4 or out.shape[0] != 1 or not out.is_contiguous():
@@ -361,6 +371,12 @@ def gather_row_ranges(out: torch.Tensor, pieces_per_rank: list[list[Piece]], gro
     _, H, S, D = out.shape
     flat = out.view(-1)
     spans = [_flat_span(p, S, D) for p in pieces_per_rank]
+    if dist.get_backend(group) == "nccl":
+        # uneven all-gather straight into the output (NCCL runs it as one
+        # group of broadcasts, one per rank's range)
+        parts = [flat[sp[0]:sp[1]] if sp else flat[:0] for sp in spans]
+        dist.all_gather(parts, parts[rank], group=group)
+        return out
     ops = []
     mine = spans[rank]
     for peer in range(world):
