@@ -1091,7 +1091,7 @@ def main():
                     help="head -> rank map for N>1 with --partition heads (minference.sharding)")
     ap.add_argument("--sim-world", type=int, default=0,
                     help="diagnostic: on one GPU, time only rank --sim-rank's compute of a "
-                         "--sim-world-GPU tile partition (no exchange)")
+                         "--sim-world-GPU partition (--partition; no exchange)")
     ap.add_argument("--sim-rank", type=int, default=0)
     ap.add_argument("--partition", default="heads", choices=["heads", "tiles"],
                     help="N>1: whole heads per rank (heads, cost-balanced map), or (head, "
@@ -1137,9 +1137,13 @@ def main():
     # the attention of the rest.
     tiles = world > 1 and args.o_proj == "none" and args.partition == "tiles"
     split_gather = world > 1 and args.o_proj == "none" and not tiles
-    if args.sim_world > 1:  # one GPU computes rank sim_rank's share of a sim_world-GPU step
+    if args.sim_world > 1 and args.partition == "tiles":
+        # one GPU computes rank sim_rank's share of a sim_world-GPU step
         tiles = True
         layer = TileLayer(args.sim_rank, args.sim_world, S, device, args.pattern, args.heads)
+    elif args.sim_world > 1:
+        layer = Layer(args.sim_rank, args.sim_world, S, device, args.pattern, args.heads,
+                      head_map_for(args.sim_world, args.pattern, args.heads, args.head_map, S))
     elif tiles:
         layer = TileLayer(rank, world, S, device, args.pattern, args.heads)
     else:

@@ -79,6 +79,15 @@ const char* mi_version(void);
  * wait) and clears it.  Synchronises the current device. */
 int mi_get_device_error(int* code);
 
+/* Self-test of the kernels' bounded waits (no counterpart in the reference):
+ * a one-block kernel arms an mbarrier for a transaction that never arrives,
+ * polls it at most spin_limit times, gives up, records device error code 120
+ * (read and cleared by mi_get_device_error), writes 1 to *gave_up (a device
+ * int) and returns.  Every wait in the attention kernels follows the same
+ * pattern with a limit of 2^26 polls: a wait that runs out records its code
+ * and the kernel unwinds instead of hanging.  Nothing faults or traps. */
+int mi_selftest_wait_timeout(uint32_t spin_limit, int* gave_up, void* stream);
+
 /* stream_llm: a query at absolute position i (= S_k - S_q + row) sees keys
  * j <= i with j < n_init or j > i - n_local.  Dense causal attention is the
  * special case n_init = 0, n_local >= S_k.  Sink and window are handled in one

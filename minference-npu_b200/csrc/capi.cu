@@ -9,6 +9,25 @@ int launch_attention(const mi_tensor4& q, const mi_tensor4& k, const mi_tensor4&
                      cudaStream_t stream);
 }  // namespace mib200
 
+namespace mib200 {
+// Self-test of the bounded wait: one thread arms an mbarrier for 16 bytes of
+// transaction that nothing delivers, waits at most `limit` polls, records
+// kSelftestWaitCode in the device error word and returns; the other threads
+// of the block wait for it at __syncthreads and return too.
+constexpr int kSelftestWaitCode = 120;
+__global__ void selftest_wait_kernel(uint32_t limit, int* waited_out) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    mbar_arrive_expect_tx(&bar, 16);
+    const bool done = mbar_wait_limit(&bar, 0, kSelftestWaitCode, limit);
+    *waited_out = done ? 0 : 1;
+  }
+  __syncthreads();
+}
+}  // namespace mib200
+
 using namespace mib200;
 
 extern "C" const char* mi_version(void) { return "minference-b200 0.1.0 (sm_100a)"; }
@@ -71,4 +90,10 @@ extern "C" int mi_dense_fwd(mi_tensor4 q, mi_tensor4 k, mi_tensor4 v, mi_tensor4
   prm.n_local = S_k + 1 + (causal ? 0 : S_q);
   prm.scale_log2 = softmax_scale * 1.4426950408889634f;
   return launch_attention(q, k, v, out, D, dtype, prm, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mi_selftest_wait_timeout(uint32_t spin_limit, int* gave_up, void* stream) {
+  if (!gave_up) return MI_ERR_SHAPE;
+  selftest_wait_kernel<<<1, 64, 0, reinterpret_cast<cudaStream_t>(stream)>>>(spin_limit, gave_up);
+  return cudaGetLastError() == cudaSuccess ? MI_OK : MI_ERR_LAUNCH;
 }

@@ -98,13 +98,17 @@ __device__ __forceinline__ bool mbar_test_wait_p(uint64_t* bar, uint32_t parity)
 // first probed with test_wait (a couple of cycles when it has already
 // completed, where a try_wait costs ~170 cycles on sm_100), then waited for
 // with try_wait, which lets the thread sleep until the phase flips.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int code,
+                                                uint32_t limit) {
   if (mbar_test_wait_p(bar, parity)) return true;
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+  for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
   }
   record_error(code);
   return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+  return mbar_wait_limit(bar, parity, code, kSpinLimit);
 }
 
 // ---------------------------------------------------------------------------

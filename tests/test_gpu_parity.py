@@ -334,3 +334,29 @@ def test_vs_convert_bit_exact(cuda, S, nv, ns, seqlen):
     ref = O.vs_convert_indexes([seqlen], v.numpy(), s.numpy(), S)
     for a, r in zip(got, ref):
         assert np.array_equal(a.cpu().numpy(), r)
+
+
+def test_bounded_wait_gives_up_and_reports(cuda):
+    """A wait that can never complete gives up after its poll limit, records
+    its code in the device error word and returns; the context stays usable
+    (the next kernels run and the error word reads clean afterwards)."""
+    import ctypes
+
+    from minference import _native
+
+    lib = _native.lib()
+    lib.mi_selftest_wait_timeout.argtypes = [ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p]
+    lib.mi_selftest_wait_timeout.restype = ctypes.c_int
+    assert _native.device_error() == 0
+    flag = torch.zeros(1, dtype=torch.int32, device=cuda)
+    rc = lib.mi_selftest_wait_timeout(1000, flag.data_ptr(),
+                                      torch.cuda.current_stream(cuda).cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(flag.item()) == 1
+    assert _native.device_error() == 120
+    assert _native.device_error() == 0  # read-and-clear
+    q, k, v = gen_qkv(1, 1, 256, 96, torch.bfloat16, 1, device=cuda)
+    out = _ops().streaming_forward(q, k, v, 16, 64)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all() and _native.device_error() == 0
