@@ -51,6 +51,9 @@ __device__ __forceinline__ int split_row(int L) {
   return ((L & 31) < 16) ? (L >> 5) * 16 + (L & 15) : 64 + (L >> 5) * 16 + (L & 15);
 }
 
+#ifndef MI_PLAN_AHEAD
+#define MI_PLAN_AHEAD 1
+#endif
 template <typename DT, int D, bool SPLIT, bool GATHER>
 __global__ void __launch_bounds__(kThreads, 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -191,20 +194,40 @@ __global__ void __launch_bounds__(kThreads, 2)
       const long long row0 = (long long)b * p.grow_b + (long long)hv * p.grow_h;
       auto gather_rows = [&](uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int g) {
         const int4* cols = reinterpret_cast<const int4*>(gcols + g * 64);
+        // all 16 loads first: the TMA issues below are ordered memory
+        // operations, so a load placed between them would wait out its full
+        // latency before the next issue
+        int4 cv[kBN / 4];
+#pragma unroll
+        for (int rg = 0; rg < kBN / 4; ++rg) cv[rg] = cols[rg];
+#pragma unroll
         for (int rg = 0; rg < kBN / 4; ++rg) {
-          const int4 c = cols[rg];
+          const int4 c = cv[rg];
           const int r0 = (int)(row0 + max(c.x, 0)), r1 = (int)(row0 + max(c.y, 0));
           const int r2 = (int)(row0 + max(c.z, 0)), r3 = (int)(row0 + max(c.w, 0));
           for (int cc = 0; cc < NC; ++cc)
             tma_gather4_2d(dst + cc * (kBN * 64) + rg * 256, map, bar, cc * 32, r0, r1, r2, r3);
         }
       };
-      auto load_k = [&](int j) -> bool {
+      // Key blocks of the entries, read kAhead entries before they are needed
+      // (a plan entry is a global load; read at the point of use its latency
+      // would stall every load issue).
+      constexpr int kAhead = MI_PLAN_AHEAD;
+      int2 ahead[kAhead + 1];  // entries j-1 .. j+kAhead-1 of the current step
+      auto fetch = [&](int j) -> int2 {
+        int2 r = make_int2(0, 0);
+        if (j >= 0 && j < n_entries) {
+          uint64_t m0, m1;
+          src.get(j, r.x, r.y, m0, m1);
+        }
+        return r;
+      };
+#pragma unroll
+      for (int i = 0; i <= kAhead; ++i) ahead[i] = fetch(i - 1);
+      auto load_k = [&](int j, int2 e) -> bool {
         const int st = j % KS, use = j / KS;
         if (use > 0 && !mbar_wait(&k_empty[st], (use - 1) & 1, 101)) return false;
-        int kb[2];
-        uint64_t m0, m1;
-        src.get(j, kb[0], kb[1], m0, m1);
+        const int kb[2] = {e.x, e.y};
         uint8_t* dst = smem + L::kKOff + st * L::kKStage;
         mbar_arrive_expect_tx(&k_full[st], L::kKStage);
         if (GATHER && kb[0] < 0) {
@@ -217,12 +240,10 @@ __global__ void __launch_bounds__(kThreads, 2)
                         kb[hb] * kBN, hv, b);
         return true;
       };
-      auto load_v = [&](int j) -> bool {
+      auto load_v = [&](int j, int2 e) -> bool {
         const int st = j % VS, use = j / VS;
         if (use > 0 && !mbar_wait(&v_empty[st], (use - 1) & 1, 103)) return false;
-        int kb[2];
-        uint64_t m0, m1;
-        src.get(j, kb[0], kb[1], m0, m1);
+        const int kb[2] = {e.x, e.y};
         uint8_t* dst = smem + L::kVOff + st * L::kVStage;
         mbar_arrive_expect_tx(&v_full[st], L::NB * L::kKVBytes);
         if (GATHER && kb[0] < 0) {
@@ -238,10 +259,13 @@ __global__ void __launch_bounds__(kThreads, 2)
       bool ok = true;
       for (int j = 0; ok && j < n_entries; ++j) {
         if (*abort_flag) break;
-        ok = load_k(j);
-        if (ok && j >= 1) ok = load_v(j - 1);
+        ok = load_k(j, ahead[1]);
+        if (ok && j >= 1) ok = load_v(j - 1, ahead[0]);
+#pragma unroll
+        for (int i = 0; i < kAhead; ++i) ahead[i] = ahead[i + 1];
+        ahead[kAhead] = fetch(j + kAhead);
       }
-      if (ok && n_entries > 0 && !*abort_flag) ok = load_v(n_entries - 1);
+      if (ok && n_entries > 0 && !*abort_flag) ok = load_v(n_entries - 1, ahead[0]);
       if (!ok) *abort_flag = 1;
     }
   } else if (warp == 5) {
