@@ -1257,11 +1257,15 @@ def main():
     pin_k = layer.k.cpu().pin_memory()
     pin_v = layer.v.cpu().pin_memory()
     e_steps = max(2, min(args.steps, 5))
-    if world == 1 and args.o_proj == "none" and not args.sim_world:
+    if args.o_proj == "none" and not tiles and not args.sim_world:
+        # every rank streams its own heads from pinned host memory and writes
+        # their output to pinned host memory (N>1: the output lands in host
+        # memory, so no NVLink exchange is part of this step)
         from minference.host_pipeline import layer_attention_from_host
 
         pin_o = torch.empty(tuple(layer.q.shape), dtype=torch.bfloat16).pin_memory()
-        e2e_mode = "host_pipeline (copies overlapped with attention, 2-head chunks)"
+        e2e_mode = ("host_pipeline (copies overlapped with attention, 2-head chunks"
+                    + (", each rank its own heads)" if world > 1 else ")"))
 
         def e2e_step():
             layer_attention_from_host(pin_q, pin_k, pin_v, pin_o, layer.run_spec, device)
