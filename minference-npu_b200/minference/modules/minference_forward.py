@@ -248,22 +248,8 @@ def attention_heads(self, q, k, v):
         else:
             # one launch over the group through a head table: no gather of
             # q/k/v and no scatter of the output
-            _run_pattern(key, q, k, v, out=out, heads=_head_table(heads, q.device))
+            _run_pattern(key, q, k, v, out=out, heads=heads)
     return out_bshd
-
-
-_HEAD_TABLES: dict = {}
-
-
-def _head_table(heads, device):
-    """Device int32 head table, cached per (heads, device): a layer's groups
-    are the same at every forward."""
-    key = (tuple(heads), str(device))
-    t = _HEAD_TABLES.get(key)
-    if t is None:
-        t = torch.tensor(heads, dtype=torch.int32, device=device)
-        _HEAD_TABLES[key] = t
-    return t
 
 
 def minference_forward():

@@ -106,18 +106,32 @@ def row_window(rows, S: int) -> tuple[int, int]:
     return r0, r1
 
 
+_HEAD_TABLES: dict = {}
+
+
 def head_table(heads, q: torch.Tensor):
     """(device int32 table or None, number of heads the call addresses).
 
-    ``heads`` lists heads of q's head dimension (a sequence or an integer
-    tensor); the op then runs on those heads only, in place, with one launch
-    (the kernels index the views through the table)."""
+    ``heads`` lists heads of q's head dimension (a sequence of ints, or an
+    integer tensor); the op then runs on those heads only, in place, with one
+    launch (the kernels index the views through the table).  A sequence is
+    checked on the host and its device table cached, so repeated calls (a
+    layer's groups at every forward) neither copy nor synchronise; a tensor is
+    checked on its device."""
     H = q.shape[1]
     if heads is None:
         return None, H
-    t = torch.as_tensor(heads, dtype=torch.int32).flatten()
-    if t.numel() == 0:
-        return t.to(q.device), 0
-    if bool((t < 0).any()) or bool((t >= H).any()):
-        raise ValueError(f"heads must lie in [0, {H}); got {t.tolist()}")
-    return t.to(q.device), int(t.numel())
+    if isinstance(heads, torch.Tensor):
+        t = heads.to(device=q.device, dtype=torch.int32).flatten()
+        if t.numel() and (bool((t < 0).any()) or bool((t >= H).any())):
+            raise ValueError(f"heads must lie in [0, {H}); got {t.tolist()}")
+        return t, int(t.numel())
+    hs = tuple(int(h) for h in heads)
+    if any(h < 0 or h >= H for h in hs):
+        raise ValueError(f"heads must lie in [0, {H}); got {list(hs)}")
+    key = (hs, str(q.device))
+    t = _HEAD_TABLES.get(key)
+    if t is None:
+        t = torch.tensor(hs, dtype=torch.int32, device=q.device)
+        _HEAD_TABLES[key] = t
+    return t, len(hs)
