@@ -1089,6 +1089,8 @@ def main():
                          "the whole gather (serial) or chunk by chunk behind it (overlap)")
     ap.add_argument("--head-map", default="balanced", choices=["balanced", "contiguous"],
                     help="head -> rank map for N>1 with --partition heads (minference.sharding)")
+    ap.add_argument("--no-graph", dest="graph", action="store_false",
+                    help="N=1: time eager steps instead of replaying the step as a CUDA graph")
     ap.add_argument("--sim-world", type=int, default=0,
                     help="diagnostic: on one GPU, time only rank --sim-rank's compute of a "
                          "--sim-world-GPU partition (--partition; no exchange)")
@@ -1227,6 +1229,19 @@ def main():
     vis_pairs = layer.visible_pairs()
     alg_flops_rank = 4.0 * D * vis_pairs
 
+    # ---- one layer step as a CUDA graph (N=1): every launch of the step is
+    # recorded once and replayed, so host-side launch work (argument checks,
+    # tensor-map encoding, workspace allocation) leaves the timed loop; the
+    # kernels and their arguments are the same as in an eager step.
+    graph = None
+    if world == 1 and args.graph and not args.sim_world:
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        graph.replay()
+        torch.cuda.synchronize()
+
     # ---- timed region (device-resident inputs) -----------------------------------
     clocks = ClockSampler(local_rank)
     clocks.start()
@@ -1238,14 +1253,23 @@ def main():
     t_lo = time.time()
     t0.record()
     for _ in range(args.steps):
-        step(ev=evs)
+        if graph is not None:
+            graph.replay()
+        else:
+            step(ev=evs)
     t1.record()
     barrier()
     t_hi = time.time()
     clk = clocks.stop(t_lo, t_hi)  # samples inside the timed region only
     ms = t0.elapsed_time(t1) / args.steps
     ms = max_over_ranks(ms)
-    attn_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+    if graph is not None:  # attention-phase events: eager steps after the timed loop
+        for _ in range(max(1, min(args.steps, 5))):
+            step(ev=evs)
+        torch.cuda.synchronize()
+        attn_ms = sum(a.elapsed_time(b) for a, b in evs) / max(1, min(args.steps, 5))
+    else:
+        attn_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
     dense_flops = dense_causal_flops(S, n_heads)
     value = dense_flops / (ms * 1e-3) / 1e12
 
@@ -1392,6 +1416,7 @@ def main():
                     "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "mode": e2e_mode},
             "gpu_launches": layer.launches_per_step() * args.steps,
+            "cuda_graph": graph is not None,
             "device_error": err,
         }
         if cpu_base is not None:
