@@ -313,6 +313,7 @@ class Layer:
         for p, hs in self.groups:
             self.slices.append((p, slice(h0, h0 + len(hs))))
             h0 += len(hs)
+        self.rep_bases, self.rep_from = None, 0  # output replicas (peer gather)
         self.local_vs = (local_vs_indices(len(self.heads), S, device)
                          if any(p == "vs_local" for p, _ in self.groups) else None)
         # the same groups as (pattern key, local heads), the dispatcher's format
@@ -329,24 +330,27 @@ class Layer:
         v = self.v if v is None else v
         for p, sl in self.slices:
             qs, ks, vs, os_ = q[:, sl], k[:, sl], v[:, sl], self.out[:, sl]
+            # peer gather: the same slice of every other rank's gather buffer
+            rp = ([b + (os_.data_ptr() - self.rep_from) for b in self.rep_bases]
+                  if self.rep_bases else None)
             if p == "vertical_and_slash":
                 vi, si = ops.vertical_and_slash_estimate(qs, ks, VS_V, VS_S)
                 a = self._ev(ev)
-                ops.vertical_slash_sparse_attention(qs, ks, vs, vi, si, out=os_)
+                ops.vertical_slash_sparse_attention(qs, ks, vs, vi, si, out=os_, out_replicas=rp)
             elif p == "block_sparse":
                 idx = ops.select_block_sparse_topk_indices(qs, ks, BS_TOPK)
                 a = self._ev(ev)
-                ops.block_sparse_attention_from_indices(qs, ks, vs, idx, out=os_)
+                ops.block_sparse_attention_from_indices(qs, ks, vs, idx, out=os_, out_replicas=rp)
             elif p == "stream_llm":
                 a = self._ev(ev)
-                ops.streaming_forward(qs, ks, vs, ST_INIT, ST_LOCAL, out=os_)
+                ops.streaming_forward(qs, ks, vs, ST_INIT, ST_LOCAL, out=os_, out_replicas=rp)
             elif p == "vs_local":
                 a = self._ev(ev)
                 ops.vertical_slash_sparse_attention(qs, ks, vs, self.local_vs[0][:, sl],
                                                     self.local_vs[1][:, sl], out=os_)
             else:
                 a = self._ev(ev)
-                ops.dense_attention(qs, ks, vs, out=os_)
+                ops.dense_attention(qs, ks, vs, out=os_, out_replicas=rp)
             if ev is not None:
                 b = torch.cuda.Event(enable_timing=True)
                 b.record()
@@ -823,14 +827,18 @@ def time_reference_cpu(S: int, steps: int, warmup: int, layer=None):
 
 def bench_config(args, S: int, world: int) -> dict:
     tiles = world > 1 and args.o_proj == "none" and args.partition == "tiles"
-    split_gather = world > 1 and args.o_proj == "none" and not tiles
+    peer = world > 1 and args.o_proj == "none" and not tiles and args.gather == "peer"
+    split_gather = world > 1 and args.o_proj == "none" and not tiles and not peer
     if tiles:
         par, gather, hmap = (f"tile-shard{world}",
                              "row ranges exchanged point to point in two halves, the first "
                              "overlapped with the remaining attention", "tiles")
     else:
         par = f"head-shard{world}" if world > 1 else "single"
-        gather = ("all-gather in two halves by local head, the first overlapped with the "
+        gather = ("attention kernels store every output tile into every GPU's buffer over "
+                  "NVLink (CUDA IPC peer buffers), one small all-reduce per step as the fence"
+                  if peer else
+                  "all-gather in two halves by local head, the first overlapped with the "
                   "remaining attention" if split_gather else
                   ("one all-gather" if world > 1 else "none"))
         hmap = args.head_map if world > 1 else "single"
@@ -1089,6 +1097,10 @@ def main():
                          "the whole gather (serial) or chunk by chunk behind it (overlap)")
     ap.add_argument("--head-map", default="balanced", choices=["balanced", "contiguous"],
                     help="head -> rank map for N>1 with --partition heads (minference.sharding)")
+    ap.add_argument("--gather", default="nccl", choices=["peer", "nccl"],
+                    help="N>1 whole-head partition: attention kernels store their output "
+                         "tiles into every GPU's buffer over NVLink (peer), or NCCL all-gathers "
+                         "the outputs in two halves (nccl)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="N=1: time eager steps instead of replaying the step as a CUDA graph")
     ap.add_argument("--sim-world", type=int, default=0,
@@ -1138,7 +1150,8 @@ def main():
     # local head), the first half as soon as its heads are done, overlapping
     # the attention of the rest.
     tiles = world > 1 and args.o_proj == "none" and args.partition == "tiles"
-    split_gather = world > 1 and args.o_proj == "none" and not tiles
+    peer = world > 1 and args.o_proj == "none" and not tiles and args.gather == "peer"
+    split_gather = world > 1 and args.o_proj == "none" and not tiles and not peer
     if args.sim_world > 1 and args.partition == "tiles":
         # one GPU computes rank sim_rank's share of a sim_world-GPU step
         tiles = True
@@ -1156,6 +1169,21 @@ def main():
     if world > 1 and not split_gather and not tiles:
         gathered = torch.empty((world,) + tuple(layer.out_bshd.shape), dtype=torch.bfloat16,
                                device=device)
+    peer_ok = None
+    if peer:
+        # every rank's kernels store their output tiles into every rank's
+        # rank-major gather buffer (own slot) over NVLink; one small
+        # all-reduce per step orders the readers after all ranks' kernels
+        from minference.sharding import peer_addresses
+
+        h_loc = len(layer.heads)
+        gbuf = torch.zeros((world, 1, h_loc, S, D), dtype=torch.bfloat16, device=device)
+        bases = peer_addresses(gbuf)
+        layer.out = gbuf[rank]
+        layer.out_bshd = layer.out
+        layer.rep_from = gbuf.data_ptr()
+        layer.rep_bases = [b for r, b in enumerate(bases) if r != rank]
+        fence = torch.zeros(1, device=device)
     if split_gather:
         h_loc = len(layer.heads)
         half = h_loc // 2
@@ -1174,6 +1202,10 @@ def main():
     def step(q=None, k=None, v=None, ev=None):
         if tiles:
             return layer.run(q, k, v, ev)
+        if peer:
+            layer.run(q, k, v, ev)
+            torch.distributed.all_reduce(fence)
+            return gbuf
         if split_gather:
             sent = []
 
@@ -1226,6 +1258,14 @@ def main():
         o_last = step()
     torch.cuda.synchronize()
     out_shape = tuple(o_last.shape)
+    if peer:  # the peer-written buffer must equal an NCCL all-gather of the own slots
+        chk = torch.empty_like(gbuf)
+        torch.distributed.all_gather_into_tensor(chk, gbuf[rank].contiguous())
+        torch.cuda.synchronize()
+        peer_ok = bool(torch.equal(chk, gbuf))
+        t = torch.tensor([1.0 if peer_ok else 0.0], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
+        peer_ok = bool(t.item() == 1.0)
     vis_pairs = layer.visible_pairs()
     alg_flops_rank = 4.0 * D * vis_pairs
 
@@ -1417,11 +1457,16 @@ def main():
                     "d2h_bytes_per_step": d2h, "mode": e2e_mode},
             "gpu_launches": layer.launches_per_step() * args.steps,
             "cuda_graph": graph is not None,
+            **({"peer_gather_matches_nccl": peer_ok} if peer else {}),
             "device_error": err,
         }
         if cpu_base is not None:
             line["cpu_baseline"] = cpu_base
         print(json.dumps(line), flush=True)
+    if peer:
+        from minference.sharding import close_peer_addresses
+
+        close_peer_addresses()
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

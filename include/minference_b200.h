@@ -70,7 +70,20 @@ typedef struct mi_tensor4 {
   int64_t stride_b, stride_h, stride_s, stride_d;
   const int32_t* head_index;
   int64_t head_extent;
+  /* Output replicas (for `out` of the attention entry points only; NULL / 0
+   * otherwise): n_replica (at most MI_MAX_REPLICAS) more base pointers, in a
+   * host array, of views with the same strides -- for instance the same
+   * buffer of the other GPUs of a node, opened in this process through CUDA
+   * IPC and reached over NVLink.  Every output tile is stored to `ptr` and to
+   * each replica by the kernel that computes it, so a head-sharded layer's
+   * output reaches every GPU without a separate all-gather.  The caller
+   * orders the replicas' readers after the call (e.g. with any collective
+   * on the stream after it). */
+  void* const* replica;
+  int64_t n_replica;
 } mi_tensor4;
+
+#define MI_MAX_REPLICAS 7
 
 /* Library version string. */
 const char* mi_version(void);

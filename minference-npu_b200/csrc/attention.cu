@@ -61,7 +61,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                     const __grid_constant__ CUtensorMap tm_v,
                     const __grid_constant__ CUtensorMap tm_o,
                     const __grid_constant__ CUtensorMap tm_kr,
-                    const __grid_constant__ CUtensorMap tm_vr, const AttnParams p) {
+                    const __grid_constant__ CUtensorMap tm_vr,
+                    const __grid_constant__ ReplicaMaps tm_rep, const AttnParams p) {
   using L = AttnSmem<D, SPLIT>;
   constexpr int NC = L::NC;
   constexpr int KS = L::KS, VS = L::VS;
@@ -572,6 +573,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (row == 0 && !*abort_flag) {
       for (int c = 0; c < NC; ++c)
         tma_store_4d(&tm_o, smem + L::kQOff + c * (kBM * 64), c * 32, t * kBM, hv, b);
+      // the same tile into every output replica (e.g. the peers' buffers)
+      for (int r = 0; r < p.n_replica; ++r)
+        for (int c = 0; c < NC; ++c)
+          tma_store_4d(&tm_rep.m[r], smem + L::kQOff + c * (kBM * 64), c * 32, t * kBM, hv, b);
       bulk_commit();
       bulk_wait_read0();
     }
@@ -610,12 +615,19 @@ static int launch_attn_t(const mi_tensor4& q, const mi_tensor4& k, const mi_tens
     if ((rc = make_rows_map(&tkr, k.ptr, rows, k.stride_s, D, 32)) != MI_OK) return rc;
     if ((rc = make_rows_map(&tvr, v.ptr, rows, v.stride_s, D, 32)) != MI_OK) return rc;
   }
+  ReplicaMaps trep;
+  memset(&trep, 0, sizeof(trep));
+  for (int r = 0; r < prm.n_replica; ++r) {
+    mi_tensor4 o = out;
+    o.ptr = out.replica[r];
+    if ((rc = make_bnsd_map(&trep.m[r], o, prm.B, prm.H, prm.Sq, D, 32, kBM)) != MI_OK) return rc;
+  }
   auto kern = attn_fwd_kernel<DT, D, SPLIT, GATHER>;
   const int alloc = L::kAlloc;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, alloc);
   if (e == cudaSuccess) {
     dim3 grid(prm.t_n, prm.H, prm.B);
-    kern<<<grid, kThreads, alloc, stream>>>(tq, tk, tv, to, tkr, tvr, prm);
+    kern<<<grid, kThreads, alloc, stream>>>(tq, tk, tv, to, tkr, tvr, trep, prm);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) {
@@ -634,6 +646,10 @@ int launch_attention(const mi_tensor4& q, const mi_tensor4& k, const mi_tensor4&
       out.head_index != q.head_index)
     return MI_ERR_SHAPE;
   prm.head_index = q.head_index;
+  if (out.n_replica < 0 || out.n_replica > MI_MAX_REPLICAS ||
+      (out.n_replica > 0 && !out.replica))
+    return MI_ERR_SHAPE;
+  prm.n_replica = (int)out.n_replica;
   prm.out = out.ptr;
   prm.os_b = out.stride_b;
   prm.os_h = out.stride_h;

@@ -69,6 +69,7 @@ struct AttnParams {
   long long plan_head_stride;  // mode 1: entries per (b,h)
   int split;                   // 1: split tiles (each half of the tile has its own key block)
   const int32_t* head_index;   // head table of the views, or null (see mi_tensor4)
+  int n_replica;               // output replicas (see mi_tensor4), maps in ReplicaMaps
   // mode 1, gathered key groups (vertical_and_slash): a plan entry with
   // kb = kb1 = -1 - g is group g of its tile, up to 64 scattered keys loaded
   // row by row (TMA gather4 over a 2-D row view of K and V) whose positions
@@ -143,6 +144,11 @@ struct AttnSmem {
 #ifndef MI_ONE_CTA_SPLIT
   static_assert(kTmemCols == 512 || kAlloc <= 113 * 1024, "two CTAs per SM");
 #endif
+};
+
+// Tensor maps of the output replicas (kernel parameter).
+struct ReplicaMaps {
+  CUtensorMap m[MI_MAX_REPLICAS];
 };
 
 // Entry j of the current tile (identical result in every warp that asks).

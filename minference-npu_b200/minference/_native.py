@@ -29,6 +29,7 @@ _STATUS = {
     7: "problem larger than the library's built-in scratch (allocation-free entry point)",
 }
 MI_F16, MI_BF16 = 0, 1
+MAX_REPLICAS = 7
 
 
 class MInferenceNativeError(RuntimeError):
@@ -44,6 +45,8 @@ class mi_tensor4(ctypes.Structure):
         ("stride_d", ctypes.c_int64),
         ("head_index", ctypes.c_void_p),
         ("head_extent", ctypes.c_int64),
+        ("replica", ctypes.POINTER(ctypes.c_void_p)),
+        ("n_replica", ctypes.c_int64),
     ]
 
 
@@ -110,13 +113,22 @@ def check(rc: int, what: str) -> None:
         raise MInferenceNativeError(f"{what} failed: status {rc} ({_STATUS.get(rc, 'unknown')})")
 
 
-def t4(x: torch.Tensor, heads: torch.Tensor | None = None) -> mi_tensor4:
+def t4(x: torch.Tensor, heads: torch.Tensor | None = None, replicas=None) -> mi_tensor4:
     """View descriptor of a BNSD tensor; `heads` (device int32) selects the
-    heads a call addresses (see mi_tensor4 in the header)."""
+    heads a call addresses; `replicas` (output only) lists device addresses of
+    the same view in other buffers, written as well (see mi_tensor4 in the
+    header)."""
     s = x.stride()
-    if heads is None:
-        return mi_tensor4(x.data_ptr(), s[0], s[1], s[2], s[3], None, 0)
-    return mi_tensor4(x.data_ptr(), s[0], s[1], s[2], s[3], heads.data_ptr(), x.shape[1])
+    hp, he = (None, 0) if heads is None else (heads.data_ptr(), x.shape[1])
+    t = mi_tensor4(x.data_ptr(), s[0], s[1], s[2], s[3], hp, he, None, 0)
+    if replicas:
+        if len(replicas) > MAX_REPLICAS:
+            raise ValueError(f"at most {MAX_REPLICAS} output replicas")
+        arr = (ctypes.c_void_p * len(replicas))(*[int(r) for r in replicas])
+        t.replica = ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p))
+        t.n_replica = len(replicas)
+        t._keep = arr  # the host array must outlive the call
+    return t
 
 
 def dtype_code(x: torch.Tensor) -> int:

@@ -94,6 +94,17 @@ def output(out: torch.Tensor | None, shape: tuple, like: torch.Tensor,
     return out
 
 
+def replica_ptrs(out_replicas, out: torch.Tensor, D: int, dk: int):
+    """Device addresses of the output view's replicas: ``out_replicas`` gives,
+    per replica, the address of element 0 of ``out`` in that buffer (an int),
+    or a tensor laid out like ``out``."""
+    if not out_replicas:
+        return None
+    if dk != D:
+        raise NotImplementedError("output replicas need a head dim of 64, 96 or 128")
+    return [int(r.data_ptr()) if isinstance(r, torch.Tensor) else int(r) for r in out_replicas]
+
+
 def row_window(rows, S: int) -> tuple[int, int]:
     """Validate an optional query-row window ``(row_begin, row_end)``: whole
     128-row tiles, except that it may end at S.  None means every row."""

@@ -15,7 +15,7 @@ import torch
 
 from .. import _native
 from ._common import (check_qkv, default_softmax_scale, head_table, kernel_dim, prepare,
-                      reference_padded_dim, row_window)
+                      reference_padded_dim, replica_ptrs, row_window)
 from ._common import output as _common_out
 
 __all__ = [
@@ -73,7 +73,7 @@ def block_sparse_attention_from_indices(q: torch.Tensor, k: torch.Tensor, v: tor
                                         softmax_scale: float | None = None, *,
                                         out: torch.Tensor | None = None,
                                         rows: tuple[int, int] | None = None,
-                                        heads=None) -> torch.Tensor:
+                                        heads=None, out_replicas=None) -> torch.Tensor:
     """Block-sparse causal attention over given key blocks ``[B,H,ceil(S/64),topk]``.
 
     ``rows=(begin, end)`` computes only those query rows (whole 128-row tiles,
@@ -99,8 +99,8 @@ def block_sparse_attention_from_indices(q: torch.Tensor, k: torch.Tensor, v: tor
     ws = _native.workspace(_native.lib().mi_block_sparse_fwd_workspace_size(B, H, S, topk), q.device)
     with torch.cuda.device(q.device):
         rc = _native.lib().mi_block_sparse_fwd_rows(
-            _native.t4(qp, tbl), _native.t4(kp, tbl), _native.t4(vp, tbl), _native.t4(out, tbl),
-            B, H, S, dk,
+            _native.t4(qp, tbl), _native.t4(kp, tbl), _native.t4(vp, tbl),
+            _native.t4(out, tbl, replica_ptrs(out_replicas, out, D, dk)), B, H, S, dk,
             _native.dtype_code(q), idx.data_ptr(), topk, scale, r0, r1, ws.data_ptr(), ws.numel(),
             _native.stream_ptr(q.device),
         )
@@ -111,9 +111,11 @@ def block_sparse_attention_from_indices(q: torch.Tensor, k: torch.Tensor, v: tor
 def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, topk_blocks: int,
                            block_size: int = _DEFAULT_BLOCK_SIZE, *,
                            out: torch.Tensor | None = None,
-                           rows: tuple[int, int] | None = None, heads=None) -> torch.Tensor:
+                           rows: tuple[int, int] | None = None, heads=None,
+                           out_replicas=None) -> torch.Tensor:
     """Block-sparse causal attention; same signature and semantics as the reference."""
     check_qkv(q, k, v)
     topk = max(1, int(topk_blocks))
     idx = select_block_sparse_topk_indices(q, k, topk, block_size, heads=heads)
-    return block_sparse_attention_from_indices(q, k, v, idx, out=out, rows=rows, heads=heads)
+    return block_sparse_attention_from_indices(q, k, v, idx, out=out, rows=rows, heads=heads,
+                                               out_replicas=out_replicas)

@@ -19,14 +19,14 @@ import torch
 
 from .. import _native
 from ._common import (check_qkv, default_softmax_scale, head_table, kernel_dim, prepare,
-                      row_window)
+                      replica_ptrs, row_window)
 from ._common import output as _common_out
 
 __all__ = ["streaming_forward", "dense_attention"]
 
 
 def _launch(q, k, v, n_init: int, n_local: int, scale: float,
-            out: torch.Tensor | None = None, heads=None) -> torch.Tensor:
+            out: torch.Tensor | None = None, heads=None, out_replicas=None) -> torch.Tensor:
     check_qkv(q, k, v)
     B, H, S_q, D = q.shape
     S_k = k.shape[2]
@@ -40,7 +40,8 @@ def _launch(q, k, v, n_init: int, n_local: int, scale: float,
         with torch.cuda.device(q.device):
             rc = _native.lib().mi_stream_fwd(
                 _native.t4(qp, tbl), _native.t4(kp, tbl), _native.t4(vp, tbl),
-                _native.t4(out, tbl), B, G, S_q, S_k, dk, _native.dtype_code(q), int(n_init),
+                _native.t4(out, tbl, replica_ptrs(out_replicas, out, D, dk)), B, G, S_q, S_k,
+                dk, _native.dtype_code(q), int(n_init),
                 int(n_local), float(scale), _native.stream_ptr(q.device),
             )
         _native.check(rc, "mi_stream_fwd")
@@ -62,14 +63,18 @@ def _window(q, k, v, out, rows):
 
 def streaming_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_init: int,
                       n_local: int, *, out: torch.Tensor | None = None,
-                      rows: tuple[int, int] | None = None, heads=None) -> torch.Tensor:
+                      rows: tuple[int, int] | None = None, heads=None,
+                      out_replicas=None) -> torch.Tensor:
     """Sink + sliding-window causal attention on BNSD ``[B,H,S,D]`` inputs.
 
     ``rows=(begin, end)`` (full prefill only) computes only those query rows
     (whole 128-row tiles, the end may be S); other output rows are left as
     they are.  ``heads`` (indices into the head dimension) runs only those
     heads, in one launch, writing them in place into ``out`` (the other heads
-    are left as they are; a new output is zero there).
+    are left as they are; a new output is zero there).  ``out_replicas``
+    (with ``out``) are addresses of the same view in other buffers -- e.g. the
+    peers' copies of the layer output -- that every output tile is also
+    written to.
 
     Same signature and result as the reference.  The reference zero-pads D to
     the next supported head dim before anything else (streaming_kernel_npu.py:
@@ -81,6 +86,8 @@ def streaming_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_init:
     n_local = int(n_local)
     scale = default_softmax_scale(q.shape[-1])
     if rows is not None:
+        if out_replicas:
+            raise NotImplementedError("rows= with output replicas")
         qw, kw, vw, full, ow = _window(q, k, v, out, rows)
         if qw.shape[2]:
             if k.shape[2] <= n_local:  # the short-circuit is decided on the whole sequence
@@ -89,14 +96,16 @@ def streaming_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_init:
                 _launch(qw, kw, vw, n_init, n_local, scale, ow, heads)
         return full
     if k.shape[2] <= n_local:
-        return dense_attention(q, k, v, scale=scale, causal=True, out=out, heads=heads)
-    return _launch(q, k, v, n_init, n_local, scale, out, heads)
+        return dense_attention(q, k, v, scale=scale, causal=True, out=out, heads=heads,
+                               out_replicas=out_replicas)
+    return _launch(q, k, v, n_init, n_local, scale, out, heads, out_replicas)
 
 
 def dense_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
                     scale: float | None = None, causal: bool = True,
                     out: torch.Tensor | None = None,
-                    rows: tuple[int, int] | None = None, heads=None) -> torch.Tensor:
+                    rows: tuple[int, int] | None = None, heads=None,
+                    out_replicas=None) -> torch.Tensor:
     """Dense attention on BNSD ``[B,H,S,D]`` inputs (MInference-NPU
     minference/backend_npu/attention.py:192-211): ``scale`` defaults to
     ``1/sqrt(D)`` of the unpadded head dim; ``causal`` masks bottom-right
@@ -105,6 +114,8 @@ def dense_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     caller-owned ``[B,H,S_q,D]`` view written in place.  ``rows`` and ``heads``
     restrict the call as in ``streaming_forward``."""
     if rows is not None:
+        if out_replicas:
+            raise NotImplementedError("rows= with output replicas")
         if not causal:
             raise NotImplementedError("rows= is for causal prefill")
         qw, kw, vw, full, ow = _window(q, k, v, out, rows)
@@ -125,8 +136,9 @@ def dense_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
         with torch.cuda.device(q.device):
             rc = _native.lib().mi_dense_fwd(
                 _native.t4(qp, tbl), _native.t4(kp, tbl), _native.t4(vp, tbl),
-                _native.t4(out, tbl), B, G, S_q, S_k, dk, _native.dtype_code(q),
-                1 if causal else 0, sc, _native.stream_ptr(q.device),
+                _native.t4(out, tbl, replica_ptrs(out_replicas, out, D, dk)), B, G, S_q, S_k,
+                dk, _native.dtype_code(q), 1 if causal else 0, sc,
+                _native.stream_ptr(q.device),
             )
         _native.check(rc, "mi_dense_fwd")
     return out[..., :D] if dk != D else out

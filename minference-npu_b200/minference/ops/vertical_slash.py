@@ -16,7 +16,7 @@ import torch
 
 from .. import _native
 from ._common import (check_qkv, default_softmax_scale, head_table, kernel_dim, prepare,
-                      row_window)
+                      replica_ptrs, row_window)
 from ._common import output as _common_out
 
 __all__ = [
@@ -62,7 +62,7 @@ def vertical_slash_sparse_attention(query: torch.Tensor, key: torch.Tensor, valu
                                     softmax_scale: float | None = None, *,
                                     out: torch.Tensor | None = None,
                                     rows: tuple[int, int] | None = None,
-                                    heads=None) -> torch.Tensor:
+                                    heads=None, out_replicas=None) -> torch.Tensor:
     """Vertical-slash causal attention; same signature as the reference op.
 
     ``rows=(begin, end)`` computes only those query rows (whole 128-row tiles,
@@ -90,8 +90,8 @@ def vertical_slash_sparse_attention(query: torch.Tensor, key: torch.Tensor, valu
     ws = _native.workspace(_native.lib().mi_vs_sparse_fwd_workspace_size(B, H, S), query.device)
     with torch.cuda.device(query.device):
         rc = _native.lib().mi_vs_sparse_fwd_rows(
-            _native.t4(qp, tbl), _native.t4(kp, tbl), _native.t4(vp, tbl), _native.t4(out, tbl),
-            B, H, S, dk,
+            _native.t4(qp, tbl), _native.t4(kp, tbl), _native.t4(vp, tbl),
+            _native.t4(out, tbl, replica_ptrs(out_replicas, out, D, dk)), B, H, S, dk,
             _native.dtype_code(query), vi.data_ptr(), vi.shape[-1], si.data_ptr(), si.shape[-1],
             scale, r0, r1, ws.data_ptr(), ws.numel(), _native.stream_ptr(query.device),
         )
@@ -101,11 +101,12 @@ def vertical_slash_sparse_attention(query: torch.Tensor, key: torch.Tensor, valu
 
 def vertical_and_slash(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, vertical_size: int,
                        slash_size: int, *, out: torch.Tensor | None = None,
-                       rows: tuple[int, int] | None = None, heads=None) -> torch.Tensor:
+                       rows: tuple[int, int] | None = None, heads=None,
+                       out_replicas=None) -> torch.Tensor:
     """Estimate indices from the last 64 queries, then run the sparse attention."""
     v_idx, s_idx = vertical_and_slash_estimate(q, k, vertical_size, slash_size, heads=heads)
     return vertical_slash_sparse_attention(q, k, v, v_idx, s_idx, out=out, rows=rows,
-                                           heads=heads)
+                                           heads=heads, out_replicas=out_replicas)
 
 
 def convert_vertical_slash_indexes(seqlens: torch.Tensor, vertical_indexes: torch.Tensor,

@@ -30,7 +30,8 @@ import torch.distributed as dist
 
 __all__ = ["head_range", "gather_heads", "head_cost", "balanced_head_map",
            "gather_heads_mapped", "o_proj_input_permutation", "gather_o_proj",
-           "tile_costs", "tile_partition", "Piece", "unit_range_split", "gather_row_ranges"]
+           "tile_costs", "tile_partition", "Piece", "unit_range_split", "gather_row_ranges",
+           "peer_addresses", "close_peer_addresses"]
 
 
 def head_range(num_heads: int, rank: int, world: int) -> range:
@@ -391,3 +392,79 @@ def gather_row_ranges(out: torch.Tensor, pieces_per_rank: list[list[Piece]], gro
         for w in dist.batch_isend_irecv(ops):
             w.wait()
     return out
+
+
+# ---------------------------------------------------------------------------
+# Peer buffers (CUDA IPC) for output replicas
+# ---------------------------------------------------------------------------
+_opened: dict = {}
+
+
+def _check(err, what):
+    from cuda.bindings import runtime as rt
+
+    if err != rt.cudaError_t.cudaSuccess:
+        raise RuntimeError(f"{what} failed: {err}")
+
+
+def peer_addresses(buf: torch.Tensor, group=None) -> list[int]:
+    """Device addresses, valid on this process's GPU, of every rank's `buf`
+    (rank order; this rank's entry is ``buf.data_ptr()``).
+
+    Every rank passes its own tensor of the same shape (collective call).
+    Each rank exports the CUDA IPC handle of the allocation holding its
+    buffer, the handles and offsets are exchanged over the process group, and
+    each peer's allocation is opened into this GPU's address space (reached
+    over NVLink / NVSwitch).  The addresses serve as output replicas of the
+    attention ops (``out_replicas=``), whose kernels then store each output
+    tile into every rank's buffer.  Every rank must keep `buf` alive until all
+    ranks have called `close_peer_addresses`."""
+    from cuda.bindings import driver as cu
+    from cuda.bindings import runtime as rt
+
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    if not buf.is_cuda:
+        raise ValueError("peer_addresses needs a CUDA tensor")
+    dev = buf.device.index if buf.device.index is not None else torch.cuda.current_device()
+    (err,) = rt.cudaSetDevice(dev)
+    _check(err, f"cudaSetDevice({dev})")
+    err, handle = rt.cudaIpcGetMemHandle(buf.data_ptr())
+    _check(err, "cudaIpcGetMemHandle")
+    err, base, _size = cu.cuMemGetAddressRange(cu.CUdeviceptr(buf.data_ptr()))
+    if err != cu.CUresult.CUDA_SUCCESS:
+        raise RuntimeError(f"cuMemGetAddressRange failed: {err}")
+    off = buf.data_ptr() - int(base)
+    infos = [None] * world
+    dist.all_gather_object(infos, (bytes(handle.reserved), off), group=group)
+    addrs = []
+    for r, (h, o) in enumerate(infos):
+        if r == rank:
+            addrs.append(buf.data_ptr())
+            continue
+        key = (dev, h)
+        if key not in _opened:
+            hs = rt.cudaIpcMemHandle_t()
+            hs.reserved = h
+            err, ptr = rt.cudaIpcOpenMemHandle(hs, rt.cudaIpcMemLazyEnablePeerAccess)
+            _check(err, f"cudaIpcOpenMemHandle (rank {r})")
+            _opened[key] = int(ptr)
+        addrs.append(_opened[key] + o)
+    return addrs
+
+
+def close_peer_addresses(group=None) -> None:
+    """Unmap every peer allocation opened by `peer_addresses` (after this
+    process's kernels that write them have finished), then wait for all
+    ranks, so that no rank frees a buffer another still maps."""
+    from cuda.bindings import runtime as rt
+
+    torch.cuda.synchronize()
+    for (dev, _), ptr in list(_opened.items()):
+        (err,) = rt.cudaSetDevice(dev)
+        _check(err, f"cudaSetDevice({dev})")
+        (err,) = rt.cudaIpcCloseMemHandle(ptr)
+        _check(err, "cudaIpcCloseMemHandle")
+    _opened.clear()
+    if dist.is_initialized():
+        dist.barrier(group=group)
