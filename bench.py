@@ -1097,7 +1097,7 @@ def main():
                          "the whole gather (serial) or chunk by chunk behind it (overlap)")
     ap.add_argument("--head-map", default="balanced", choices=["balanced", "contiguous"],
                     help="head -> rank map for N>1 with --partition heads (minference.sharding)")
-    ap.add_argument("--gather", default="nccl", choices=["peer", "nccl"],
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="N>1 whole-head partition: attention kernels store their output "
                          "tiles into every GPU's buffer over NVLink (peer), or NCCL all-gathers "
                          "the outputs in two halves (nccl)")
