@@ -21,6 +21,10 @@ the layer's (head, 128-row tile) units into contiguous per-rank ranges of
 equal modelled cost; a rank then runs row windows (``rows=``) of a few heads,
 and `gather_row_ranges` re-assembles the ``[B, H, S, D]`` output, in which
 each rank's range is one contiguous block of memory.
+
+Without any collective for the data: `peer_addresses` opens the other
+ranks' output buffers (CUDA IPC) so the attention kernels can store their
+tiles into them directly (the ops' ``out_replicas=``).
 """
 
 from __future__ import annotations
