@@ -1178,12 +1178,28 @@ def main():
 
         h_loc = len(layer.heads)
         gbuf = torch.zeros((world, 1, h_loc, S, D), dtype=torch.bfloat16, device=device)
-        bases = peer_addresses(gbuf)
-        layer.out = gbuf[rank]
-        layer.out_bshd = layer.out
-        layer.rep_from = gbuf.data_ptr()
-        layer.rep_bases = [b for r, b in enumerate(bases) if r != rank]
-        fence = torch.zeros(1, device=device)
+        try:
+            bases = peer_addresses(gbuf)
+            ok_t = torch.ones(1, device=device)
+        except RuntimeError as exc:  # no CUDA IPC between these GPUs: NCCL instead
+            print(f"[rank {rank}] peer buffers unavailable ({exc}); using the NCCL gather",
+                  file=sys.stderr, flush=True)
+            bases, ok_t = None, torch.zeros(1, device=device)
+        torch.distributed.all_reduce(ok_t, op=torch.distributed.ReduceOp.MIN)
+        if ok_t.item() == 1.0:
+            layer.out = gbuf[rank]
+            layer.out_bshd = layer.out
+            layer.rep_from = gbuf.data_ptr()
+            layer.rep_bases = [b for r, b in enumerate(bases) if r != rank]
+            fence = torch.zeros(1, device=device)
+        else:
+            from minference.sharding import close_peer_addresses
+
+            close_peer_addresses()
+            peer, split_gather = False, True
+            args.gather = "nccl"
+            layer = Layer(rank, world, S, device, args.pattern, args.heads, head_map,
+                          head_major_out=True)
     if split_gather:
         h_loc = len(layer.heads)
         half = h_loc // 2
