@@ -161,3 +161,29 @@ def test_vs_local_slashes_scattered_verticals(cuda, S, nv, ns):
         ref = torch.softmax(logits.masked_fill(~mask, float("-inf")), -1) @ v[0, h].float()
         err = (out[0, h].float() - ref).abs().max().item()
         assert err < TOL, f"head {h}: {err}"
+
+
+@pytest.mark.parametrize("S,D,dt", [(65536, 96, torch.float16), (32768, 128, torch.bfloat16),
+                                    (32768, 64, torch.float16)])
+def test_other_dtypes_and_head_dims_large(cuda, S, D, dt):
+    """fp16 and head dims 64 / 128 at long context: both index kernels bit exact
+    against the C oracle, block_sparse and stream_llm attention on sampled rows."""
+    ops, O = _ops(), _oracle()
+    pd = 64 if D <= 64 else 128
+    q, k, v = gen_qkv(1, 1, S, D, dt, S + D, lowrank=2.0, sinks=16)
+    qd, kd, vd = q.to(cuda), k.to(cuda), v.to(cuda)
+    vi, si = ops.vertical_and_slash_estimate(qd, kd, 1000, 6096)
+    rv, rs = O.vs_estimate(q, k, 1000, 6096)
+    assert np.array_equal(vi.cpu().numpy(), rv) and np.array_equal(si.cpu().numpy(), rs)
+    idx = ops.select_block_sparse_topk_indices(qd, kd, 64)
+    ref_idx = O.block_pool_topk(q, k, 64, pd ** -0.5)
+    assert np.array_equal(idx.cpu().numpy(), ref_idx)
+    rows = torch.tensor(_rows(S, 100, D), device=cuda)
+    out = ops.block_sparse_attention_from_indices(qd, kd, vd, idx)
+    ref = ref_rows(qd[0, 0], kd[0, 0], vd[0, 0], rows,
+                   lambda r: O.block_sparse_rows_mask(ref_idx[0, 0], S, r.cpu().numpy()), pd ** -0.5)
+    assert (out[0, 0][rows].float() - ref).abs().max().item() < TOL
+    out = ops.streaming_forward(qd, kd, vd, 128, 1024)
+    ref = ref_rows(qd[0, 0], kd[0, 0], vd[0, 0], rows,
+                   lambda r: O.stream_rows_mask(r.cpu().numpy(), S, S, 128, 1024), pd ** -0.5)
+    assert (out[0, 0][rows].float() - ref).abs().max().item() < TOL
