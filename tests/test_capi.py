@@ -76,6 +76,19 @@ def test_argument_validation_without_device(lib):
     assert lib.mi_vs_estimate(t, t, 1, 1, 128, 96, 1, 200, 50, 0.1, None, None, None, 0, None) == 1
     assert lib.mi_vs_sparse_fwd(t, t, t, t, 1, 1, 128, 96, 1, None, 1, None, 1, 1.0, None, 0,
                                 None) == 3
+    # dense: causal rows need keys; more than MI_MAX_REPLICAS output replicas
+    # or mismatched head tables are refused before any launch
+    assert lib.mi_dense_fwd(t, t, t, t, 1, 1, 32, 16, 96, 1, 1, 1.0, None) == 1
+    assert lib.mi_dense_fwd(t, t, t, t, 1, 1, 16, 16, 96, 5, 1, 1.0, None) == 2
+    import ctypes
+
+    arr = (ctypes.c_void_p * 8)(*([16] * 8))
+    o = _native.mi_tensor4(0, 0, 0, 0, 1, None, 0, ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p)), 8)
+    assert lib.mi_dense_fwd(t, t, t, o, 1, 1, 16, 16, 96, 1, 1, 1.0, None) == 1
+    hq = _native.mi_tensor4(0, 0, 0, 0, 1, 64, 4, None, 0)
+    assert lib.mi_dense_fwd(hq, t, t, t, 1, 1, 16, 16, 96, 1, 1, 1.0, None) == 1
+    assert lib.mi_block_sparse_fwd_rows(t, t, t, t, 1, 1, 1000, 96, 1, None, 4, 1.0, 100, 500,
+                                        None, 0, None) == 1  # row window not tile aligned
 
 
 def test_ops_refuse_cpu_tensors():
