@@ -83,8 +83,14 @@ struct AttnParams {
 
 constexpr int kBM = 128;       // query rows per CTA
 constexpr int kBN = 64;        // keys per KV block
-constexpr int kKStages = 3;    // K ring depth (K runs ahead of V)
-constexpr int kVStages = 3;    // V ring depth
+#ifndef MI_KSTAGES
+#define MI_KSTAGES 3
+#endif
+#ifndef MI_VSTAGES
+#define MI_VSTAGES 3
+#endif
+constexpr int kKStages = MI_KSTAGES;  // K ring depth (K runs ahead of V)
+constexpr int kVStages = MI_VSTAGES;  // V ring depth
 constexpr int kThreads = 192;
 
 // Ring depths.  A split tile stages two key blocks per entry (one per query
